@@ -1,0 +1,511 @@
+#!/usr/bin/env python
+"""Benchmark of the DoRA hot path on B200: one adapted linear layer, forward + backward.
+
+Workload (the high-rank single-layer configuration): W0 [28672 x 8192] bf16
+~N(0, 0.02), rank 384, A kaiming-uniform, B ~N(0, 0.01), scale 1.0, X
+[16384 x 8192] bf16 ~N(0, 1), seeded synthetic data.  One step is
+    y = base(x) + DoRA delta   (factored norm + fused compose)
+    y.backward(dy)             (fused compose backward, LoRA and base GEMMs)
+through ``dorafactors_b200.layer.DoraLinear``, i.e. the PEFT wiring of
+``DoraLinearLayer``.  The metric is whole-job tokens/s; the line also carries
+the factored norm's tensor TFLOP/s and the compose kernels' HBM GB/s against
+the measured peaks, each timed with CUDA events around every native call of
+the timed steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+N > 1 (launched by torchrun, one process per GPU): token data parallelism.
+Every rank runs the full layer on its own 16384 tokens (weak scaling) and the
+LoRA / magnitude gradients are all-reduced over NCCL each step, the exchange
+data-parallel training performs.  ``--impl reference`` times the CPU
+restatement of the reference's eager path (the oracle) on the host cores, on a
+bounded token sample of the same workload, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+OUT_F, IN_F, RANK, TOKENS, SCALE = 28672, 8192, 384, 16384, 1.0
+METRIC = "DoRA layer fwd+bwd tokens/s, norm TFLOP/s & compose HBM GB/s vs peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+CPU_SAMPLE_TOKENS = 128
+
+
+def workload_config(parallelism: str) -> dict:
+    return {
+        "workload": f"dora_linear_fwd_bwd out={OUT_F} in={IN_F} r={RANK} tokens={TOKENS}/rank bf16",
+        "out_features": OUT_F,
+        "in_features": IN_F,
+        "rank": RANK,
+        "tokens_per_rank": TOKENS,
+        "scale": SCALE,
+        "l2": "inputs larger than L2 (x 268 MB, each activation 940 MB), no flush needed",
+        "parallelism": parallelism,
+    }
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+# Algorithmic work per native call (bf16, e = 2 bytes).
+def compose_fwd_bytes(T, out, e=2):
+    return e * 4 * T * out + e * out  # read lora, base, g; write out, inner
+
+
+def compose_bwd_bytes(T, out, e=2):
+    return e * 4 * T * out + 2 * e * out  # read d_out, inner, g; write d_lora, d_base, d_g
+
+
+def norm_flops(out, inp, r):
+    return 2 * out * inp * r + 2 * r * r * inp + 2 * out * r * r  # W0 A^T, A A^T, B G
+
+
+def norm_bytes(out, inp, r, e=2):
+    return e * (out * inp + r * inp + out * r) + e * out  # read W0, A, B; write the norm
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self._t is not None:
+            self._t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p.strip() for p in vis.split(",") if p.strip()]
+        if local_rank < len(parts) and parts[local_rank].isdigit():
+            return int(parts[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------------------
+# Per-call CUDA-event timing of the native entry points
+# ---------------------------------------------------------------------------
+class NativeTimer:
+    """Wraps the native calls with CUDA events on the current stream while enabled."""
+
+    NAMES = ("weight_norm", "compose_fwd", "compose_bwd")
+
+    def __init__(self):
+        import torch
+
+        from dorafactors_b200 import _native
+
+        self.torch = torch
+        self.native = _native
+        self.enabled = False
+        self.events: dict = {n: [] for n in self.NAMES}
+        self.orig = {n: getattr(_native, n) for n in self.NAMES}
+        for n in self.NAMES:
+            setattr(_native, n, self._wrap(n, self.orig[n]))
+
+    def _wrap(self, name, fn):
+        def wrapped(*a, **k):
+            if not self.enabled:
+                return fn(*a, **k)
+            s = self.torch.cuda.Event(enable_timing=True)
+            e = self.torch.cuda.Event(enable_timing=True)
+            s.record()
+            r = fn(*a, **k)
+            e.record()
+            self.events[name].append((s, e))
+            return r
+
+        return wrapped
+
+    def summary(self) -> dict:
+        out = {}
+        for n, evs in self.events.items():
+            if evs:
+                ms = [s.elapsed_time(e) for s, e in evs]
+                out[n] = {"calls": len(ms), "avg_ms": sum(ms) / len(ms), "total_ms": sum(ms)}
+        return out
+
+    def restore(self):
+        for n in self.NAMES:
+            setattr(self.native, n, self.orig[n])
+
+
+# ---------------------------------------------------------------------------
+# Native arm
+# ---------------------------------------------------------------------------
+def build_layer(device, seed):
+    import math
+
+    import torch
+    from torch import nn
+
+    from dorafactors_b200.layer import DoraLinear
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    base = nn.Linear(IN_F, OUT_F, bias=False, device=device, dtype=torch.bfloat16)
+    with torch.no_grad():
+        base.weight.copy_((torch.randn(OUT_F, IN_F, device=device, generator=g) * 0.02).bfloat16())
+    mod = DoraLinear(base, r=RANK, scaling=SCALE, init_lora_B_zero=False)
+    with torch.no_grad():
+        bound = 1.0 / math.sqrt(IN_F)  # kaiming_uniform(a=sqrt(5)) bound for fan_in = IN_F
+        mod.lora_A.weight.copy_(((torch.rand(RANK, IN_F, device=device, generator=g) * 2 - 1) * bound).bfloat16())
+        mod.lora_B.weight.copy_((torch.randn(OUT_F, RANK, device=device, generator=g) * 0.01).bfloat16())
+        mod.reset_magnitude()
+    x = torch.randn(TOKENS, IN_F, device=device, generator=g).bfloat16()
+    dy = torch.randn(TOKENS, OUT_F, device=device, generator=g).bfloat16()
+    return mod, x, dy
+
+
+def run_native(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from dorafactors_b200 import _native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    torch.backends.cuda.matmul.allow_tf32 = False
+
+    mod, x_dev, dy = build_layer(device, 1234 + rank)
+    x = x_dev.clone().requires_grad_(True)
+    params = [mod.lora_A.weight, mod.lora_B.weight, mod.lora_magnitude_vector.weight]
+
+    def allreduce_grads():
+        if world > 1:
+            for p in params:
+                dist.all_reduce(p.grad)
+
+    def step(xin):
+        for p in params:
+            p.grad = None
+        xin.grad = None
+        y = mod(xin)
+        y.backward(dy)
+        allreduce_grads()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    timer = NativeTimer()
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(physical_gpu_index(local_rank))
+    clocks.start()
+    launches0 = _native.launch_count()
+    timer.enabled = True
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    t0.record()
+    for _ in range(args.steps):
+        step(x)
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    timer.enabled = False
+    launches = _native.launch_count() - launches0
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    kern = timer.summary()
+    peak_mem = torch.cuda.max_memory_allocated(device)
+
+    # End to end through the public API: pinned host input copied in and the
+    # magnitude gradient read back inside the timed region, every step.
+    x_host = x_dev.detach().cpu().pin_memory()
+    x_e2e = torch.empty_like(x_dev).requires_grad_(True)
+    dm_host = torch.empty(OUT_F, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        with torch.no_grad():
+            x_e2e.copy_(x_host, non_blocking=True)
+        step(x_e2e)
+        dm_host.copy_(mod.lora_magnitude_vector.weight.grad, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        kernels = {}
+        if "compose_fwd" in kern:
+            a = compose_fwd_bytes(TOKENS, OUT_F) / (kern["compose_fwd"]["avg_ms"] * 1e-3) / 1e9
+            kernels["compose_fwd"] = {**kern["compose_fwd"], "achieved_gbs": a, "frac": a / peaks["hbm_gbs"]}
+        if "compose_bwd" in kern:
+            a = compose_bwd_bytes(TOKENS, OUT_F) / (kern["compose_bwd"]["avg_ms"] * 1e-3) / 1e9
+            kernels["compose_bwd"] = {**kern["compose_bwd"], "achieved_gbs": a, "frac": a / peaks["hbm_gbs"]}
+        if "weight_norm" in kern:
+            a = norm_flops(OUT_F, IN_F, RANK) / (kern["weight_norm"]["avg_ms"] * 1e-3) / 1e12
+            kernels["weight_norm"] = {**kern["weight_norm"], "achieved_tflops": a,
+                                      "frac": a / peaks["bf16_tflops"]}
+        dom = max(kern, key=lambda n: kern[n]["total_ms"]) if kern else None
+        roof = None
+        if dom in ("compose_fwd", "compose_bwd"):
+            nbytes = compose_fwd_bytes(TOKENS, OUT_F) if dom == "compose_fwd" else compose_bwd_bytes(TOKENS, OUT_F)
+            roof = {"kernel": dom, "bound": "hbm", "achieved": kernels[dom]["achieved_gbs"],
+                    "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": kernels[dom]["frac"],
+                    "traffic": read_traffic(dom), "algorithmic_bytes": nbytes, "peak_source": peak_src}
+        elif dom == "weight_norm":
+            roof = {"kernel": dom, "bound": "tensor", "achieved": kernels[dom]["achieved_tflops"],
+                    "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": kernels[dom]["frac"],
+                    "traffic": read_traffic(dom), "algorithmic_flops": norm_flops(OUT_F, IN_F, RANK),
+                    "peak_source": peak_src}
+        value = TOKENS * world / (ms * 1e-3)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded normal / kaiming-uniform weights, normal tokens)",
+            "config": workload_config("single" if world == 1 else f"dp{world}"),
+            "roofline": roof,
+            "kernels": kernels,
+            "e2e": {"value": TOKENS * world / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": TOKENS * IN_F * 2, "d2h_bytes_per_step": OUT_F * 2},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "peak_mem_gb": peak_mem / 1e9,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample()
+        print(json.dumps(line), flush=True)
+    timer.restore()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def read_traffic(kernel: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists for this kernel."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    try:
+        with open(p) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == kernel:
+                    return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle (numpy restatement of the eager path)
+# ---------------------------------------------------------------------------
+def _cpu_inputs(tokens: int, seed: int = 0):
+    """Seeded bf16-valued inputs as float32 numpy arrays (generated with torch for speed)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+
+    def bf(t):
+        return t.bfloat16().float().numpy()
+
+    W = bf(torch.randn(OUT_F, IN_F, generator=g) * 0.02)
+    A = bf((torch.rand(RANK, IN_F, generator=g) * 2 - 1) / IN_F**0.5)
+    B = bf(torch.randn(OUT_F, RANK, generator=g) * 0.01)
+    x = bf(torch.randn(tokens, IN_F, generator=g))
+    dy = bf(torch.randn(tokens, OUT_F, generator=g))
+    return W, A, B, x, dy
+
+
+def cpu_step(W, A, B, x, dy, m):
+    from oracle import dora_oracle as orc
+
+    t0 = time.perf_counter()
+    orc.dora_linear_forward_backward(x, W, None, A, B, m, SCALE, dy, "bf16")
+    return time.perf_counter() - t0
+
+
+def cpu_norm(W, A, B):
+    from oracle import dora_oracle as orc
+
+    t0 = time.perf_counter()
+    n, _ = orc.weight_norm_factored(W, A, B, SCALE, "bf16")
+    return time.perf_counter() - t0, n
+
+
+def cpu_tokens_per_s(t_norm: float, t_step: float) -> float:
+    """Full-workload tokens/s extrapolated from one norm over the full weight and a
+    forward+backward on CPU_SAMPLE_TOKENS tokens (which also recomputes the norm)."""
+    t_tok = max(t_step - t_norm, 1e-9)
+    full = t_norm + t_tok * (TOKENS / CPU_SAMPLE_TOKENS)
+    return TOKENS / full
+
+
+def cpu_baseline_sample() -> dict:
+    W, A, B, x, dy = _cpu_inputs(CPU_SAMPLE_TOKENS)
+    t_norm, m = cpu_norm(W, A, B)
+    t_step = cpu_step(W, A, B, x, dy, m)
+    return {
+        "value": cpu_tokens_per_s(t_norm, t_step),
+        "unit": "tokens/s",
+        "cores": os.cpu_count(),
+        "kind": "port",
+        "sample": (f"numpy oracle of the reference eager path: factored norm over the full "
+                   f"{OUT_F}x{IN_F} r={RANK} weight ({t_norm:.2f} s) + one forward/backward on "
+                   f"{CPU_SAMPLE_TOKENS} tokens ({t_step:.2f} s incl. its norm), extrapolated to "
+                   f"{TOKENS} tokens"),
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    W, A, B, x, dy = _cpu_inputs(CPU_SAMPLE_TOKENS)
+    _, m = cpu_norm(W, A, B)
+    for _ in range(args.warmup):
+        cpu_step(W, A, B, x, dy, m)
+    norms, steps = [], []
+    for _ in range(args.steps):
+        tn, _ = cpu_norm(W, A, B)
+        norms.append(tn)
+        steps.append(cpu_step(W, A, B, x, dy, m))
+    t_norm, t_step = statistics.median(norms), statistics.median(steps)
+    value = cpu_tokens_per_s(t_norm, t_step)
+    ms = TOKENS / value * 1e3
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded normal / uniform weights, normal tokens)",
+        "config": workload_config("single"),
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": (f"each step: numpy oracle norm over the full weight + forward/backward on "
+                                    f"{CPU_SAMPLE_TOKENS} tokens, extrapolated to {TOKENS} tokens")},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core oracle sample")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,222 @@
+"""ctypes binding of ``libdora_b200.so`` (the C ABI declared in ``include/dora_b200.h``).
+
+This is the only place Python touches the native library.  Every wrapper takes
+CUDA tensors, checks what the C side cannot (device, dtype, contiguity), passes
+raw pointers plus the current CUDA stream, and turns a non-zero status into the
+Python exception the reference raises for the same condition.  There is no
+fallback: if the library is missing or a tensor is not on a CUDA device, the
+call fails loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdora_b200.so")
+
+DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNSUPPORTED = 2
+ERR_WORKSPACE = 3
+ERR_CUDA = 4
+ERR_DEVICE_TIMEOUT = 5
+
+# Every symbol the header declares, with its ctypes signature.
+_i64, _vp, _sz, _int, _dbl = ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_double
+SIGNATURES = {
+    "dora_version": (_int, []),
+    "dora_status_string": (ctypes.c_char_p, [_int]),
+    "dora_last_cuda_error": (ctypes.c_char_p, []),
+    "dora_launch_count": (ctypes.c_ulonglong, []),
+    "dora_device_error": (_int, [_int, ctypes.POINTER(_int)]),
+    "dora_compose_fwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _int, _vp]),
+    "dora_compose_bwd_workspace_size": (_sz, [_i64, _i64, _int]),
+    "dora_compose_bwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
+    "dora_norm_assembly": (_int, [_vp, _vp, _vp, _dbl, _vp, _i64, _vp]),
+    "dora_weight_norm_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int]),
+    "dora_weight_norm": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _int, _dbl, _vp, _vp, _vp, _sz, _vp]),
+    "dora_weight_norm_dense": (_int, [_vp, _vp, _i64, _i64, _int, _int, _dbl, _vp, _vp]),
+}
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+class DoraNativeError(RuntimeError):
+    """A native DoRA call failed (CUDA error, device timeout or workspace problem)."""
+
+
+def load_library(path: str | None = None) -> ctypes.CDLL:
+    """Load the native library once; raise ImportError if it has not been built."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise ImportError(
+                f"{p} is missing: build it with `python -m dorafactors_b200.build` (nvcc, sm_100a). "
+                "The DoRA hot path has no non-native fallback."
+            )
+        lib = ctypes.CDLL(p)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def status_string(code: int) -> str:
+    return load_library().dora_status_string(code).decode()
+
+
+def check(code: int, what: str) -> None:
+    """Map a dora_status_t to the exception type the reference uses for that condition."""
+    if code == OK:
+        return
+    lib = load_library()
+    msg = f"{what}: {lib.dora_status_string(code).decode()}"
+    if code == ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    if code == ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    if code == ERR_CUDA:
+        raise DoraNativeError(f"{msg} ({lib.dora_last_cuda_error().decode()})")
+    raise DoraNativeError(msg)
+
+
+def device_error(reset: bool = True) -> int:
+    """Synchronise and return (then clear) the device-side error word."""
+    out = ctypes.c_int(0)
+    check(load_library().dora_device_error(1 if reset else 0, ctypes.byref(out)), "dora_device_error")
+    return out.value
+
+
+def launch_count() -> int:
+    """Kernels launched by the native library so far in this process."""
+    return int(load_library().dora_launch_count())
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype} (expected float32, float16 or bfloat16)") from None
+
+
+def require_cuda(*tensors: torch.Tensor, what: str) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                f"{what}: tensors must be on a CUDA device (got {t.device}); "
+                "the B200 DoRA path has no CPU implementation"
+            )
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{what}: tensors on different devices ({dev} vs {t.device})")
+    return dev
+
+
+def stream_ptr(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr() if t is not None else None)
+
+
+# ---------------------------------------------------------------------------
+# Workspace for the backward's column reduction.  Its leading counters must be
+# zero before first use and are left zero by every call, so one zero-filled
+# buffer is kept per (device, stream) and grown when a larger shape arrives.
+# ---------------------------------------------------------------------------
+_ws_cache: dict = {}
+_ws_lock = threading.Lock()
+
+
+def bwd_workspace(device: torch.device, rows: int, cols: int, act_code: int) -> tuple[torch.Tensor | None, int]:
+    need = load_library().dora_compose_bwd_workspace_size(rows, cols, act_code)
+    if need == 0:
+        return None, 0
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < need:
+            buf = torch.zeros(need, dtype=torch.uint8, device=device)
+            _ws_cache[key] = buf
+    return buf, buf.numel()
+
+
+def clear_workspace_cache() -> None:
+    with _ws_lock:
+        _ws_cache.clear()
+
+
+# ---------------------------------------------------------------------------
+# Thin wrappers (2-D contiguous views; shape logic lives in dora_fused.py)
+# ---------------------------------------------------------------------------
+def compose_fwd(lora2d, base2d, g1d, scale: float, out2d, inner2d) -> None:
+    dev = lora2d.device
+    rows, cols = lora2d.shape
+    code = load_library().dora_compose_fwd(
+        ptr(lora2d), ptr(base2d), ptr(g1d), dtype_code(g1d), float(scale), ptr(out2d), ptr(inner2d),
+        rows, cols, dtype_code(lora2d), stream_ptr(dev),
+    )
+    check(code, "dora_compose_fwd")
+
+
+def compose_bwd(d_out2d, inner2d, g1d, scale: float, d_lora2d, d_base2d, d_g1d) -> None:
+    dev = d_out2d.device
+    rows, cols = d_out2d.shape
+    act = dtype_code(d_out2d)
+    ws, nbytes = (None, 0)
+    if d_g1d is not None:
+        ws, nbytes = bwd_workspace(dev, rows, cols, act)
+    code = load_library().dora_compose_bwd(
+        ptr(d_out2d), ptr(inner2d), ptr(g1d), dtype_code(g1d), float(scale), ptr(d_lora2d), ptr(d_base2d),
+        ptr(d_g1d), ptr(ws), nbytes, rows, cols, act, stream_ptr(dev),
+    )
+    check(code, "dora_compose_bwd")
+
+
+def norm_assembly(w, c, b, scale: float, out) -> None:
+    code = load_library().dora_norm_assembly(ptr(w), ptr(c), ptr(b), float(scale), ptr(out), w.numel(),
+                                             stream_ptr(w.device))
+    check(code, "dora_norm_assembly")
+
+
+def weight_norm(W, A, B, scale: float, norm_out, parts=None) -> None:
+    lib = load_library()
+    out_f, in_f = W.shape
+    rank = A.shape[0]
+    wd, ad, bd = dtype_code(W), dtype_code(A), dtype_code(B)
+    need = lib.dora_weight_norm_workspace_size(out_f, in_f, rank, wd, ad, bd)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=W.device)
+    code = lib.dora_weight_norm(
+        ptr(W), ptr(A), ptr(B), out_f, in_f, rank, wd, ad, bd, float(scale), ptr(norm_out), ptr(parts),
+        ptr(ws), need, stream_ptr(W.device),
+    )
+    check(code, "dora_weight_norm")
+
+
+def weight_norm_dense(W, L, scale: float, norm_out) -> None:
+    out_f, in_f = W.shape
+    code = load_library().dora_weight_norm_dense(
+        ptr(W), ptr(L), out_f, in_f, dtype_code(W), dtype_code(L), float(scale), ptr(norm_out), stream_ptr(W.device)
+    )
+    check(code, "dora_weight_norm_dense")

@@ -1,0 +1,245 @@
+// Fused DoRA compose backward for sm_100a: one pass over d_out (and inner).
+//
+//   d_lora = (g * s) * d_out
+//   d_base = (g - 1) * d_out
+//   d_g    = sum over rows of inner * d_out        (per column)
+//
+// Same thread layout as the forward: a thread owns one 16-byte column slice
+// and walks down a strided set of rows, so g and the running d_g sums of its
+// columns live in registers.  The column sum is reduced deterministically:
+//   1. each thread accumulates its rows serially in fp32;
+//   2. the CTA folds its row-threads through shared memory in a fixed order;
+//   3. every CTA writes its column partial to the workspace, and the last CTA
+//      to finish a column tile (a completion counter, no spin-waits) folds the
+//      partials of all CTAs in blockIdx.y order and writes d_g.
+// No float atomics are used, so repeated calls give identical bits.
+#include "dora_common.cuh"
+
+namespace dora {
+
+template <typename TA, typename TG, int VEC, bool kDL, bool kDB, bool kDG>
+__global__ void __launch_bounds__(256)
+compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, const TG* __restrict__ g, float s,
+                   TA* __restrict__ d_lora, TA* __restrict__ d_base, TG* __restrict__ d_g,
+                   unsigned* __restrict__ counters, float* __restrict__ partials, int64_t rows, int64_t vcols) {
+  __shared__ float red[256 * VEC];
+  __shared__ bool is_last;
+  const int64_t vc = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool active = vc < vcols;
+  const int64_t cols = vcols * VEC;
+  float gs[VEC], gm1[VEC], acc[VEC];
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) {
+    const float gv = active ? to_f32(g[vc * VEC + k]) : 0.f;
+    gs[k] = __fmul_rn(gv, s);
+    gm1[k] = __fsub_rn(gv, 1.0f);
+    acc[k] = 0.f;
+  }
+  const int64_t row0 = int64_t(blockIdx.y) * blockDim.y + threadIdx.y;
+  const int64_t rstep = int64_t(gridDim.y) * blockDim.y;
+  constexpr int U = 4;
+  if (active) {
+    for (int64_t r = row0; r < rows; r += U * rstep) {
+      if constexpr (VEC > 1) {
+        uint4 dv[U], iv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t rr = r + u * rstep;
+          if (rr < rows) {
+            const int64_t off = rr * cols + vc * VEC;
+            dv[u] = ld_stream(d_out + off);
+            if constexpr (kDG) iv[u] = ld_stream(inner + off);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t rr = r + u * rstep;
+          if (rr < rows) {
+            const int64_t off = rr * cols + vc * VEC;
+            float df[VEC], xf[VEC], lf[VEC], bf[VEC];
+            Vec16<TA>::unpack(dv[u], df);
+            if constexpr (kDG) Vec16<TA>::unpack(iv[u], xf);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+              if constexpr (kDL) lf[k] = __fmul_rn(gs[k], df[k]);
+              if constexpr (kDB) bf[k] = __fmul_rn(gm1[k], df[k]);
+              if constexpr (kDG) acc[k] = fmaf(xf[k], df[k], acc[k]);
+            }
+            if constexpr (kDL) st_global(d_lora + off, Vec16<TA>::pack(lf));
+            if constexpr (kDB) st_global(d_base + off, Vec16<TA>::pack(bf));
+          }
+        }
+      } else {
+        float df[U], xf[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t rr = r + u * rstep;
+          if (rr < rows) {
+            df[u] = to_f32(d_out[rr * cols + vc]);
+            if constexpr (kDG) xf[u] = to_f32(inner[rr * cols + vc]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t rr = r + u * rstep;
+          if (rr < rows) {
+            if constexpr (kDL) d_lora[rr * cols + vc] = from_f32<TA>(__fmul_rn(gs[0], df[u]));
+            if constexpr (kDB) d_base[rr * cols + vc] = from_f32<TA>(__fmul_rn(gm1[0], df[u]));
+            if constexpr (kDG) acc[0] = fmaf(xf[u], df[u], acc[0]);
+          }
+        }
+      }
+    }
+  }
+  if constexpr (kDG) {
+    const int tx = threadIdx.x, ty = threadIdx.y, TX = blockDim.x, TY = blockDim.y;
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) red[(ty * TX + tx) * VEC + k] = acc[k];
+    __syncthreads();
+    if (ty == 0 && active) {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        float t = red[tx * VEC + k];
+        for (int y = 1; y < TY; ++y) t += red[(y * TX + tx) * VEC + k];
+        partials[int64_t(blockIdx.y) * cols + vc * VEC + k] = t;
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tx == 0 && ty == 0) {
+      const unsigned done = atomicAdd(&counters[blockIdx.x], 1u);
+      is_last = (done == gridDim.y - 1);
+    }
+    __syncthreads();
+    if (is_last) {
+      __threadfence();
+      if (ty == 0 && active) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+          const int64_t c = vc * VEC + k;
+          float t = 0.f;
+          for (unsigned y = 0; y < gridDim.y; ++y) t += __ldcg(partials + int64_t(y) * cols + c);
+          d_g[c] = from_f32<TG>(t);
+        }
+      }
+      if (tx == 0 && ty == 0) counters[blockIdx.x] = 0u;  // ready for the next call
+    }
+  }
+}
+
+struct BwdPlan {
+  bool vec;
+  int64_t vcols;
+  EwShape sh;
+  size_t counter_bytes, partial_bytes;
+};
+
+static BwdPlan bwd_plan(int64_t rows, int64_t cols, int esize, bool aligned) {
+  BwdPlan p;
+  const int V = 16 / esize;
+  p.vec = aligned && (cols % V == 0);
+  p.vcols = p.vec ? cols / V : cols;
+  p.sh = ew_shape(rows, p.vcols);
+  p.counter_bytes = ((size_t(p.sh.grid.x) * 4 + 255) / 256) * 256;
+  p.partial_bytes = size_t(p.sh.grid.y) * size_t(cols) * 4;
+  return p;
+}
+
+template <typename TA, typename TG, int V, bool DL, bool DB, bool DG>
+static void launch_bwd_v(const BwdPlan& p, const void* d_out, const void* inner, const void* g, float s,
+                         void* d_lora, void* d_base, void* d_g, unsigned* cnt, float* part, int64_t rows,
+                         cudaStream_t st) {
+  compose_bwd_kernel<TA, TG, V, DL, DB, DG><<<p.sh.grid, p.sh.block, 0, st>>>(
+      static_cast<const TA*>(d_out), static_cast<const TA*>(inner), static_cast<const TG*>(g), s,
+      static_cast<TA*>(d_lora), static_cast<TA*>(d_base), static_cast<TG*>(d_g), cnt, part, rows, p.vcols);
+}
+
+template <typename TA, typename TG, int V>
+static void launch_bwd_sel(const BwdPlan& p, const void* d_out, const void* inner, const void* g, float s,
+                           void* d_lora, void* d_base, void* d_g, unsigned* cnt, float* part, int64_t rows,
+                           cudaStream_t st) {
+  const int sel = (d_lora ? 4 : 0) | (d_base ? 2 : 0) | (d_g ? 1 : 0);
+#define DORA_BWD_CASE(n, a, b, c) \
+  case n: launch_bwd_v<TA, TG, V, a, b, c>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st); break;
+  switch (sel) {
+    DORA_BWD_CASE(1, false, false, true)
+    DORA_BWD_CASE(2, false, true, false)
+    DORA_BWD_CASE(3, false, true, true)
+    DORA_BWD_CASE(4, true, false, false)
+    DORA_BWD_CASE(5, true, false, true)
+    DORA_BWD_CASE(6, true, true, false)
+    DORA_BWD_CASE(7, true, true, true)
+    default: break;
+  }
+#undef DORA_BWD_CASE
+}
+
+template <typename TA, typename TG>
+static int launch_bwd(const void* d_out, const void* inner, const void* g, float s, void* d_lora, void* d_base,
+                      void* d_g, void* ws, size_t ws_bytes, int64_t rows, int64_t cols, cudaStream_t st) {
+  const bool aligned = aligned16(d_out) && (!inner || aligned16(inner)) && (!d_lora || aligned16(d_lora)) &&
+                       (!d_base || aligned16(d_base));
+  BwdPlan p = bwd_plan(rows, cols, sizeof(TA), aligned);
+  unsigned* cnt = nullptr;
+  float* part = nullptr;
+  if (d_g) {
+    if (!ws || ws_bytes < p.counter_bytes + p.partial_bytes || (reinterpret_cast<uintptr_t>(ws) & 255u))
+      return DORA_ERR_WORKSPACE;
+    cnt = static_cast<unsigned*>(ws);
+    part = reinterpret_cast<float*>(static_cast<char*>(ws) + p.counter_bytes);
+  }
+  constexpr int V = 16 / sizeof(TA);
+  if (p.vec) launch_bwd_sel<TA, TG, V>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st);
+  else launch_bwd_sel<TA, TG, 1>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st);
+  return check_launch();
+}
+
+}  // namespace dora
+
+using namespace dora;
+
+extern "C" size_t dora_compose_bwd_workspace_size(int64_t rows, int64_t cols, int act_dtype) {
+  if (rows <= 0 || cols <= 0 || !dtype_ok(act_dtype)) return 0;
+  // The unaligned plan has the most column tiles, so it bounds both layouts.
+  BwdPlan a = bwd_plan(rows, cols, dtype_size(act_dtype), true);
+  BwdPlan b = bwd_plan(rows, cols, dtype_size(act_dtype), false);
+  size_t na = a.counter_bytes + a.partial_bytes, nb = b.counter_bytes + b.partial_bytes;
+  return na > nb ? na : nb;
+}
+
+extern "C" int dora_compose_bwd(const void* d_out, const void* inner, const void* g, int g_dtype, double scale,
+                                void* d_lora, void* d_base, void* d_g, void* workspace, size_t workspace_bytes,
+                                int64_t rows, int64_t cols, int act_dtype, void* stream) {
+  if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
+  if (g_dtype != act_dtype && g_dtype != DORA_DTYPE_F32) return DORA_ERR_INVALID_ARGUMENT;
+  if (!d_lora && !d_base && !d_g) return DORA_OK;
+  if (d_g && !inner) return DORA_ERR_INVALID_ARGUMENT;
+  if (!d_out || !g) return DORA_ERR_INVALID_ARGUMENT;
+  if (rows == 0 || cols == 0) {
+    // Empty activations: the column sums are zero.
+    if (d_g && cols > 0) {
+      cudaError_t e = cudaMemsetAsync(d_g, 0, size_t(cols) * dtype_size(g_dtype), static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return set_cuda_error(e);
+    }
+    return DORA_OK;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float s = float(scale);
+  switch (act_dtype) {
+    case DORA_DTYPE_BF16:
+      return g_dtype == DORA_DTYPE_F32
+                 ? launch_bwd<__nv_bfloat16, float>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
+                                                    workspace_bytes, rows, cols, st)
+                 : launch_bwd<__nv_bfloat16, __nv_bfloat16>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
+                                                            workspace_bytes, rows, cols, st);
+    case DORA_DTYPE_F16:
+      return g_dtype == DORA_DTYPE_F32
+                 ? launch_bwd<__half, float>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes,
+                                             rows, cols, st)
+                 : launch_bwd<__half, __half>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes,
+                                              rows, cols, st);
+    default:
+      return launch_bwd<float, float>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes, rows,
+                                      cols, st);
+  }
+}

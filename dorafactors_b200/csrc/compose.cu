@@ -1,0 +1,156 @@
+// Fused DoRA compose forward for sm_100a.
+//
+//   out   = (g - 1) * base + g * (s * lora)
+//   inner = s * lora + base                      (training forward only)
+//
+// The kernel is HBM-bound (2 reads + 1 or 2 writes per element).  Each thread
+// owns one 16-byte column slice of the [rows x cols] activation and walks down
+// the rows, so the slice of g it needs is loaded once into registers and
+// reused for every row (no per-element g traffic, no index division).  A warp
+// covers 32 consecutive 16-byte slices of one row (512 contiguous bytes), and
+// four rows are in flight per thread to keep enough bytes outstanding to
+// saturate HBM3e.  The grid is sized to the SM count.
+//
+// Arithmetic is fp32 with one rounding per output; the op order is the
+// reference's ((g - 1) * base + g * (s * lora), dora_fused.py:32-54), each op
+// correctly rounded (no FMA contraction), so fp32 results are bitwise equal to
+// the reference's fp32 PyTorch evaluation.
+#include "dora_common.cuh"
+
+namespace dora {
+
+// kNc selects the read-only (non-coherent) load path; the in-place form
+// (out == lora) reads with coherent loads instead, since lora is written.
+template <typename TA, typename TG, int VEC, bool kInner, bool kNc>
+__global__ void __launch_bounds__(256)
+compose_fwd_kernel(const TA* lora, const TA* __restrict__ base, const TG* __restrict__ g,
+                   float s, TA* out, TA* __restrict__ inner, int64_t rows, int64_t vcols) {
+  const int64_t vc = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // vector column
+  if (vc >= vcols) return;
+  const int64_t cols = vcols * VEC;
+  float gv[VEC], gm1[VEC];
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) {
+    gv[k] = to_f32(g[vc * VEC + k]);
+    gm1[k] = __fsub_rn(gv[k], 1.0f);
+  }
+  const int64_t row0 = int64_t(blockIdx.y) * blockDim.y + threadIdx.y;
+  const int64_t rstep = int64_t(gridDim.y) * blockDim.y;
+  constexpr int U = 4;  // rows in flight per thread
+  for (int64_t r = row0; r < rows; r += U * rstep) {
+    if constexpr (VEC > 1) {
+      uint4 lv[U], bv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t rr = r + u * rstep;
+        if (rr < rows) {
+          const int64_t off = rr * cols + vc * VEC;
+          lv[u] = kNc ? ld_stream(lora + off) : ld_stream_coherent(lora + off);
+          bv[u] = ld_stream(base + off);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t rr = r + u * rstep;
+        if (rr < rows) {
+          const int64_t off = rr * cols + vc * VEC;
+          float lf[VEC], bf[VEC], of[VEC], inf[VEC];
+          Vec16<TA>::unpack(lv[u], lf);
+          Vec16<TA>::unpack(bv[u], bf);
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) {
+            const float sl = __fmul_rn(s, lf[k]);
+            of[k] = __fadd_rn(__fmul_rn(gm1[k], bf[k]), __fmul_rn(gv[k], sl));
+            if constexpr (kInner) inf[k] = __fadd_rn(sl, bf[k]);
+          }
+          st_global(out + off, Vec16<TA>::pack(of));
+          if constexpr (kInner) st_global(inner + off, Vec16<TA>::pack(inf));
+        }
+      }
+    } else {
+      float lf[U], bf[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t rr = r + u * rstep;
+        if (rr < rows) {
+          lf[u] = to_f32(lora[rr * cols + vc]);
+          bf[u] = to_f32(base[rr * cols + vc]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t rr = r + u * rstep;
+        if (rr < rows) {
+          const float sl = __fmul_rn(s, lf[u]);
+          out[rr * cols + vc] = from_f32<TA>(__fadd_rn(__fmul_rn(gm1[0], bf[u]), __fmul_rn(gv[0], sl)));
+          if constexpr (kInner) inner[rr * cols + vc] = from_f32<TA>(__fadd_rn(sl, bf[u]));
+        }
+      }
+    }
+  }
+}
+
+template <typename TA, typename TG>
+static int launch_compose(const void* lora, const void* base, const void* g, float s, void* out, void* inner,
+                          int64_t rows, int64_t cols, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(TA);
+  const bool vec = (cols % V == 0) && aligned16(lora) && aligned16(base) && aligned16(out) &&
+                   (inner == nullptr || aligned16(inner));
+  const int64_t vcols = vec ? cols / V : cols;
+  if (vcols > int64_t(65535) * 64) return DORA_ERR_UNSUPPORTED;
+  EwShape sh = ew_shape(rows, vcols);
+  auto L = static_cast<const TA*>(lora);
+  auto B = static_cast<const TA*>(base);
+  auto G = static_cast<const TG*>(g);
+  auto O = static_cast<TA*>(out);
+  auto I = static_cast<TA*>(inner);
+  const bool inplace = (out == lora);
+  if (vec) {
+    if (inner) compose_fwd_kernel<TA, TG, V, true, true><<<sh.grid, sh.block, 0, st>>>(L, B, G, s, O, I, rows, vcols);
+    else if (inplace) compose_fwd_kernel<TA, TG, V, false, false><<<sh.grid, sh.block, 0, st>>>(L, B, G, s, O, I, rows, vcols);
+    else compose_fwd_kernel<TA, TG, V, false, true><<<sh.grid, sh.block, 0, st>>>(L, B, G, s, O, I, rows, vcols);
+  } else {
+    if (inner) compose_fwd_kernel<TA, TG, 1, true, true><<<sh.grid, sh.block, 0, st>>>(L, B, G, s, O, I, rows, vcols);
+    else compose_fwd_kernel<TA, TG, 1, false, false><<<sh.grid, sh.block, 0, st>>>(L, B, G, s, O, I, rows, vcols);
+  }
+  return check_launch();
+}
+
+static bool ranges_overlap(const void* a, const void* b, size_t bytes) {
+  auto x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + bytes && y < x + bytes;
+}
+
+}  // namespace dora
+
+using namespace dora;
+
+extern "C" int dora_compose_fwd(const void* lora, const void* base, const void* g, int g_dtype, double scale,
+                                void* out, void* inner, int64_t rows, int64_t cols, int act_dtype,
+                                void* stream) {
+  if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
+  if (g_dtype != act_dtype && g_dtype != DORA_DTYPE_F32) return DORA_ERR_INVALID_ARGUMENT;
+  if (rows == 0 || cols == 0) return DORA_OK;
+  if (!lora || !base || !g || !out) return DORA_ERR_INVALID_ARGUMENT;
+  const size_t bytes = size_t(rows) * size_t(cols) * dtype_size(act_dtype);
+  if (inner && (ranges_overlap(inner, lora, bytes) || ranges_overlap(inner, base, bytes) ||
+                ranges_overlap(inner, out, bytes)))
+    return DORA_ERR_INVALID_ARGUMENT;
+  if (inner && out == lora) return DORA_ERR_INVALID_ARGUMENT;  // the training form is out-of-place
+  if (out != lora && ranges_overlap(out, lora, bytes)) return DORA_ERR_INVALID_ARGUMENT;
+  if (ranges_overlap(out, base, bytes)) return DORA_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float s = float(scale);
+  switch (act_dtype) {
+    case DORA_DTYPE_BF16:
+      return g_dtype == DORA_DTYPE_F32
+                 ? launch_compose<__nv_bfloat16, float>(lora, base, g, s, out, inner, rows, cols, st)
+                 : launch_compose<__nv_bfloat16, __nv_bfloat16>(lora, base, g, s, out, inner, rows, cols, st);
+    case DORA_DTYPE_F16:
+      return g_dtype == DORA_DTYPE_F32
+                 ? launch_compose<__half, float>(lora, base, g, s, out, inner, rows, cols, st)
+                 : launch_compose<__half, __half>(lora, base, g, s, out, inner, rows, cols, st);
+    default:
+      return launch_compose<float, float>(lora, base, g, s, out, inner, rows, cols, st);
+  }
+}

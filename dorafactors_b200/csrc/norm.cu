@@ -1,0 +1,194 @@
+// dora_weight_norm: plan, workspace layout and launch sequence of the
+// factored row norm (dora.py:1024-1153).
+//
+// Launches (tensor-core path, bf16 weights and adapters):
+//   1. Gram partials   G_z = A[:, Kz] A[:, Kz]^T       tcgen05, split-K, fp32 store
+//   2. Gram reduce     G = sum_z G_z; Y = G^T as fp32 and as a bf16 hi + lo pair
+//   3. cross term      rowsum(B * (W0 A^T)) and ||W0||^2   tcgen05 row-dot, split-K
+//   4. B G B^T term    rowsum(B * (B Y_hi^T + B Y_lo^T))   tcgen05 row-dot
+//   5. finalize        fixed-order partial sums + norm assembly + cast
+// fp16 runs step 4 on CUDA cores from the fp32 G (an fp16 hi/lo split could
+// overflow for large Gram entries); every other dtype mix runs steps 1, 3 and
+// 4 on CUDA cores.  The two-term split keeps about 16 significant bits of G,
+// so B G B^T carries a relative error near 2^-16 instead of bf16's 2^-8.
+#include "norm_internal.cuh"
+
+namespace dora {
+
+struct NormPlan {
+  bool tc_u, tc_v, tc_g;
+  int gram_splits, u_splits, u_ntiles, v_splits, v_ntiles;
+  size_t off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, total;
+};
+
+static size_t up256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Choose a K split so that (tiles x splits) fills the GPU in close to whole
+// waves; every split costs one extra epilogue, weighed at 2%.
+static int pick_splits(int64_t tiles, int kb_total, int sms, int max_splits) {
+  int best = 1;
+  double best_score = -1.0;
+  for (int s = 1; s <= max_splits && s <= kb_total; ++s) {
+    const double units = double(tiles) * s;
+    const double waves = double((int64_t(units) + sms - 1) / sms);
+    const double score = (units / sms) / waves * (1.0 - 0.02 * (s - 1));
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = s;
+    }
+  }
+  return best;
+}
+
+static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, int bdt, bool aligned) {
+  NormPlan p{};
+  const int sms = num_sms();
+  const bool half_uniform = (wdt == adt && adt == bdt) && (wdt == DORA_DTYPE_BF16 || wdt == DORA_DTYPE_F16);
+  p.tc_u = half_uniform && aligned && in % 8 == 0 && in > 0;
+  p.tc_g = p.tc_u;
+  p.tc_v = p.tc_u && wdt == DORA_DTYPE_BF16 && r % 8 == 0;
+  // Gram partials
+  if (p.tc_g) {
+    const TcGemmShape g = tc_gemm_shape(r, r, in);
+    const int64_t tiles = int64_t(g.m_tiles) * g.n_tiles;
+    int s = int(sms / (tiles > 0 ? tiles : 1));
+    const int cap = g.kblocks / 4 > 0 ? g.kblocks / 4 : 1;
+    p.gram_splits = s < 1 ? 1 : (s > cap ? cap : s);
+  } else {
+    const int64_t tiles = ((r + 63) / 64) * ((r + 63) / 64);
+    const int64_t kb = (in + 255) / 256;
+    int64_t s = (2 * sms) / (tiles > 0 ? tiles : 1);
+    if (s > kb) s = kb;
+    p.gram_splits = int(s < 1 ? 1 : s);
+  }
+  // Cross term
+  if (p.tc_u) {
+    const TcGemmShape u = tc_gemm_shape(out, r, in);
+    p.u_ntiles = u.n_tiles;
+    p.u_splits = pick_splits(int64_t(u.m_tiles) * u.n_tiles, u.kblocks, sms, 8);
+  } else {
+    p.u_ntiles = int((r + 63) / 64);
+    const int64_t tiles = ((out + 63) / 64) * p.u_ntiles;
+    int64_t s = (4 * sms) / (tiles > 0 ? tiles : 1);
+    const int64_t kb = (in + 255) / 256;
+    if (s > kb) s = kb;
+    p.u_splits = int(s < 1 ? 1 : s);
+  }
+  // B G B^T term
+  if (p.tc_v) {
+    const TcGemmShape v = tc_gemm_shape(out, r, r);
+    p.v_ntiles = v.n_tiles;
+    p.v_splits = pick_splits(int64_t(v.m_tiles) * v.n_tiles, 2 * v.kblocks, sms, 4);
+  } else {
+    p.v_ntiles = int((r + 63) / 64);
+    p.v_splits = 1;
+  }
+  size_t o = 0;
+  p.off_gpart = o; o += up256(size_t(p.gram_splits) * r * r * 4);
+  p.off_yt = o;    o += up256(size_t(r) * r * 4);
+  p.off_hi = o;    o += up256(size_t(r) * r * 2);
+  p.off_lo = o;    o += up256(size_t(r) * r * 2);
+  p.off_w = o;     o += up256(size_t(p.u_splits) * out * 4);
+  p.off_c = o;     o += up256(size_t(p.u_splits) * p.u_ntiles * out * 4);
+  p.off_b = o;     o += up256(size_t(p.v_splits) * p.v_ntiles * out * 4);
+  p.total = o;
+  return p;
+}
+
+}  // namespace dora
+
+using namespace dora;
+
+extern "C" size_t dora_weight_norm_workspace_size(int64_t out_features, int64_t in_features, int64_t rank,
+                                                  int w_dtype, int a_dtype, int b_dtype) {
+  if (out_features <= 0 || in_features < 0 || rank < 0) return 0;
+  if (!dtype_ok(w_dtype) || !dtype_ok(a_dtype) || !dtype_ok(b_dtype)) return 0;
+  // The aligned plan is never smaller than the unaligned one for the same shape.
+  NormPlan a = make_plan(out_features, in_features, rank, w_dtype, a_dtype, b_dtype, true);
+  NormPlan b = make_plan(out_features, in_features, rank, w_dtype, a_dtype, b_dtype, false);
+  return a.total > b.total ? a.total : b.total;
+}
+
+extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int64_t out_features,
+                                int64_t in_features, int64_t rank, int w_dtype, int a_dtype, int b_dtype,
+                                double scale, void* norm_out, float* parts, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  if (out_features < 0 || in_features < 0 || rank < 0) return DORA_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(w_dtype) || !dtype_ok(a_dtype) || !dtype_ok(b_dtype)) return DORA_ERR_INVALID_ARGUMENT;
+  if (out_features == 0) return DORA_OK;
+  if (!norm_out || (in_features > 0 && !W)) return DORA_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t M = out_features, K = in_features, R = rank;
+  const bool lora_term = scale != 0.0 && R > 0 && K > 0;
+  if (lora_term && (!A || !B)) return DORA_ERR_INVALID_ARGUMENT;
+  const bool aligned = aligned16(W) && (!lora_term || (aligned16(A) && aligned16(B)));
+  NormPlan p = make_plan(M, K, R, w_dtype, a_dtype, b_dtype, aligned);
+  if (!workspace || workspace_bytes < p.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return DORA_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  float* gpart = reinterpret_cast<float*>(ws + p.off_gpart);
+  float* yt = reinterpret_cast<float*>(ws + p.off_yt);
+  void* hi = ws + p.off_hi;
+  void* lo = ws + p.off_lo;
+  float* wpart = reinterpret_cast<float*>(ws + p.off_w);
+  float* cpart = reinterpret_cast<float*>(ws + p.off_c);
+  float* bpart = reinterpret_cast<float*>(ws + p.off_b);
+  int rc;
+
+  if (!lora_term) {
+    // ||W0|| only: the scale == 0 short-cut (dora.py:1117-1129), or no adapter rank.
+    if (K > 0) {
+      launch_row_sumsq(w_dtype, W, M, K, wpart, st);
+      if ((rc = check_launch())) return rc;
+    }
+    launch_norm_finalize(wpart, K > 0 ? 1 : 0, cpart, 0, bpart, 0, M, scale, w_dtype, norm_out, parts, st);
+    return check_launch();
+  }
+
+  // 1-2. Gram matrix G = A A^T.
+  if (p.tc_g) {
+    TcGemmArgs g{};
+    g.dtype = a_dtype; g.X = A; g.Y1 = A; g.Y2 = nullptr; g.Z = nullptr; g.ldz = 0;
+    g.M = R; g.N = R; g.K = K; g.mode = kGemmStore; g.sumsq = false; g.k_splits = p.gram_splits;
+    g.C = gpart;
+    if ((rc = tc_rowdot_gemm(g, st))) return rc;
+  } else {
+    simt_gemm<kGemmStore, false>(a_dtype, a_dtype, a_dtype, A, K, A, K, nullptr, 0, R, R, K, p.gram_splits,
+                                 nullptr, nullptr, gpart, R, st);
+    if ((rc = check_launch())) return rc;
+  }
+  launch_gram_reduce(gpart, p.gram_splits, R, yt, p.tc_v ? b_dtype : DORA_DTYPE_BF16, p.tc_v ? hi : nullptr,
+                     p.tc_v ? lo : nullptr, st);
+  if ((rc = check_launch())) return rc;
+
+  // 3. cross term + ||W0||^2.
+  if (p.tc_u) {
+    TcGemmArgs u{};
+    u.dtype = w_dtype; u.X = W; u.Y1 = A; u.Y2 = nullptr; u.Z = B; u.ldz = R;
+    u.M = M; u.N = R; u.K = K; u.mode = kGemmRowdot; u.sumsq = true; u.k_splits = p.u_splits;
+    u.rowdot_part = cpart; u.sumsq_part = wpart;
+    if ((rc = tc_rowdot_gemm(u, st))) return rc;
+  } else {
+    simt_gemm<kGemmRowdot, true>(w_dtype, a_dtype, b_dtype, W, K, A, K, B, R, M, R, K, p.u_splits, cpart, wpart,
+                                 nullptr, 0, st);
+    if ((rc = check_launch())) return rc;
+  }
+
+  // 4. B G B^T term.
+  if (p.tc_v) {
+    TcGemmArgs v{};
+    v.dtype = b_dtype; v.X = B; v.Y1 = hi; v.Y2 = lo; v.Z = B; v.ldz = R;
+    v.M = M; v.N = R; v.K = R; v.mode = kGemmRowdot; v.sumsq = false; v.k_splits = p.v_splits;
+    v.rowdot_part = bpart;
+    if ((rc = tc_rowdot_gemm(v, st))) return rc;
+  } else {
+    simt_gemm<kGemmRowdot, false>(b_dtype, DORA_DTYPE_F32, b_dtype, B, R, yt, R, B, R, M, R, R, 1, bpart, nullptr,
+                                  nullptr, 0, st);
+    if ((rc = check_launch())) return rc;
+  }
+
+  // 5. Fixed-order reduction of the partials and the norm assembly.
+  launch_norm_finalize(wpart, p.u_splits, cpart, p.u_splits * p.u_ntiles, bpart, p.v_splits * p.v_ntiles, M, scale,
+                       w_dtype, norm_out, parts, st);
+  return check_launch();
+}

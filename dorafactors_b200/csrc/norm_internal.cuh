@@ -1,0 +1,48 @@
+// Internal interfaces shared by the factored-norm translation units.
+#pragma once
+
+#include "dora_common.cuh"
+
+namespace dora {
+
+enum { kGemmRowdot = 0, kGemmStore = 1 };
+
+// CUDA-core kernels (norm_simt.cu).
+template <int MODE, bool SSQ>
+void simt_gemm(int dx, int dy, int dz, const void* X, int64_t ldx, const void* Y, int64_t ldy, const void* Z,
+               int64_t ldz, int64_t M, int64_t N, int64_t K, int ksplit, float* rowdot, float* sumsq, float* C,
+               int64_t ldc, cudaStream_t st);
+void launch_row_sumsq(int dx, const void* X, int64_t M, int64_t K, float* out, cudaStream_t st);
+void launch_gram_reduce(const float* part, int nsplit, int64_t r, float* yt, int half_dtype, void* hi, void* lo,
+                        cudaStream_t st);
+void launch_norm_finalize(const float* wpart, int nw, const float* cpart, int nc, const float* bpart, int nb,
+                          int64_t M, double scale, int out_dtype, void* norm_out, float* parts, cudaStream_t st);
+
+// Tensor-core row-dot GEMM (norm_tc.cu).
+struct TcGemmArgs {
+  int dtype;                 // DORA_DTYPE_BF16 or DORA_DTYPE_F16 (X, Y1, Y2 and Z share it)
+  const void* X;             // [M x K] row-major, ld = K
+  const void* Y1;            // [N x K] row-major, ld = K
+  const void* Y2;            // optional second Y, same shape; its k-blocks follow Y1's (X is re-read)
+  const void* Z;             // rowdot mode: [M x N] row-major, ld = ldz
+  int64_t ldz;
+  int64_t M, N, K;
+  int mode;                  // kGemmRowdot or kGemmStore
+  bool sumsq;                // also emit sum_k X[m,k]^2 (rowdot mode, n-tile 0 only)
+  int k_splits;              // contiguous K ranges per (m, n) tile
+  float* rowdot_part;        // [n_tiles * k_splits][M]
+  float* sumsq_part;         // [k_splits][M]
+  float* C;                  // store mode: [k_splits][M][N] fp32
+};
+struct TcGemmShape {
+  int nt;        // N tile (columns of TMEM used)
+  int n_tiles;
+  int m_tiles;
+  int kblocks;   // 64-wide k-blocks per Y operand
+};
+TcGemmShape tc_gemm_shape(int64_t M, int64_t N, int64_t K);
+bool tc_gemm_supported(int dtype, int64_t M, int64_t N, int64_t K, const void* X, const void* Y, const void* Z,
+                       int64_t ldz);
+int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st);
+
+}  // namespace dora

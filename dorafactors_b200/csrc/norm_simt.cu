@@ -1,0 +1,339 @@
+// Factored DoRA row norm: CUDA-core (fp32 FMA) kernels and the shared
+// reduction / assembly kernels.
+//
+// The factored norm (dora.py:1024-1153) is
+//   ||W0 + s B A||^2_row = ||W0||^2 + 2 s rowsum(B * (W0 A^T)) + s^2 rowsum((B G) * B),
+//   G = A A^T.
+// Both row sums are linear in the GEMM result, so every GEMM here is a
+// "row-dot GEMM": C = X Y^T is formed tile by tile on chip and immediately
+// contracted with Z (= B) along the row, leaving one float per row per tile.
+// Tiles along N and splits along K write separate partial vectors that the
+// finalize kernel adds in a fixed order, so the result is deterministic and
+// the [out x r] products never reach HBM.
+//
+// The tensor-core path (norm_tc.cu) replaces the GEMMs for bf16/fp16; this
+// file serves fp32 weights, mixed weight/adapter dtypes and odd alignments.
+#include "dora_common.cuh"
+#include "norm_internal.cuh"
+
+namespace dora {
+
+// ---------------------------------------------------------------------------
+// Row-dot / store GEMM on CUDA cores.  64x64 tile, BK = 16, 256 threads, each
+// thread a 4x4 sub-tile at stride 16 (conflict-free shared-memory reads).
+// grid = (ceil(N/64), ceil(M/64), ksplit).
+// ---------------------------------------------------------------------------
+template <typename TX, typename TY, typename TZ, int MODE, bool kSumSq>
+__global__ void __launch_bounds__(256)
+simt_rowdot_gemm(const TX* __restrict__ X, int64_t ldx, const TY* __restrict__ Y, int64_t ldy,
+                 const TZ* __restrict__ Z, int64_t ldz, int64_t M, int64_t N, int64_t K, int64_t kchunk,
+                 float* __restrict__ rowdot_part, float* __restrict__ sumsq_part, float* __restrict__ C,
+                 int64_t ldc) {
+  constexpr int BM = 64, BN = 64, BK = 16;
+  __shared__ float As[BK][BM + 4];
+  __shared__ float Bs[BK][BN + 4];
+  const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
+  const int64_t m0 = int64_t(blockIdx.y) * BM, n0 = int64_t(blockIdx.x) * BN;
+  const int64_t kb = int64_t(blockIdx.z) * kchunk;
+  const int64_t ke = (kb + kchunk < K) ? kb + kchunk : K;
+  float acc[4][4] = {};
+  float ssq = 0.f;
+  const bool do_ssq = kSumSq && blockIdx.x == 0;
+  for (int64_t k0 = kb; k0 < ke; k0 += BK) {
+    {  // each thread loads 4 consecutive k of one row of X and of Y
+      const int lr = t >> 2, lk = (t & 3) * 4;
+      const int64_t xm = m0 + lr, yn = n0 + lr;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int64_t k = k0 + lk + q;
+        As[lk + q][lr] = (xm < M && k < ke) ? to_f32(X[xm * ldx + k]) : 0.f;
+        Bs[lk + q][lr] = (yn < N && k < ke) ? to_f32(Y[yn * ldy + k]) : 0.f;
+      }
+    }
+    __syncthreads();
+    if (do_ssq && t < BM) {
+#pragma unroll
+      for (int k = 0; k < BK; ++k) ssq = fmaf(As[k][t], As[k][t], ssq);
+    }
+#pragma unroll
+    for (int k = 0; k < BK; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[k][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[k][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  if (do_ssq && t < BM && m0 + t < M) sumsq_part[int64_t(blockIdx.z) * M + m0 + t] = ssq;
+  if constexpr (MODE == kGemmRowdot) {
+    const int64_t p = int64_t(blockIdx.z) * gridDim.x + blockIdx.x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t m = m0 + ty + 16 * i;
+      float v = 0.f;
+      if (m < M) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t n = n0 + tx + 16 * j;
+          if (n < N) v = fmaf(acc[i][j], to_f32(Z[m * ldz + n]), v);
+        }
+      }
+      // Lanes tx = 0..15 of one half-warp hold the same row.
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (tx == 0 && m < M) rowdot_part[p * M + m] = v;
+    }
+  } else {
+    float* Cz = C + int64_t(blockIdx.z) * M * ldc;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t m = m0 + ty + 16 * i;
+      if (m >= M) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t n = n0 + tx + 16 * j;
+        if (n < N) Cz[m * ldc + n] = acc[i][j];
+      }
+    }
+  }
+}
+
+// Sum of squares of each row (scale == 0 short-cut, dora.py:1117-1129).
+template <typename TX>
+__global__ void row_sumsq_kernel(const TX* __restrict__ X, int64_t M, int64_t K, float* __restrict__ out) {
+  const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float s = 0.f;
+  for (int64_t k = lane; k < K; k += 32) {
+    const float v = to_f32(X[row * K + k]);
+    s = fmaf(v, v, s);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) out[row] = s;
+}
+
+// Gram reduction: G = sum_z Gpart[z]; writes Y = G^T in fp32 (for the
+// CUDA-core B G product) and, when hi/lo are given, the two-term split
+// Y = hi + lo with hi, lo in the half type TH (for the tensor-core product).
+template <typename TH>
+__global__ void gram_reduce_kernel(const float* __restrict__ part, int nsplit, int64_t r, float* __restrict__ yt,
+                                   TH* __restrict__ hi, TH* __restrict__ lo) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= r * r) return;
+  const int64_t i = idx / r, j = idx % r;  // output Y[i][j] = G[j][i]
+  float v = 0.f;
+  for (int z = 0; z < nsplit; ++z) v += part[int64_t(z) * r * r + j * r + i];
+  yt[idx] = v;
+  if (hi) {
+    const TH h = from_f32<TH>(v);
+    hi[idx] = h;
+    lo[idx] = from_f32<TH>(v - to_f32(h));
+  }
+}
+
+// norm[m] = sqrt(max(w + (2s) c + (s^2) b, 0)), four rounded fp32 ops in the
+// reference order (dora_fused.py:917-934), then cast to the weight dtype.
+__device__ __forceinline__ float assemble_one(float w, float c, float b, float two_s, float s2) {
+  const float t1 = __fmul_rn(two_s, c);
+  const float p = __fadd_rn(w, t1);
+  const float t2 = __fmul_rn(s2, b);
+  float n2 = __fadd_rn(p, t2);
+  n2 = (n2 > 0.f) ? n2 : ((n2 != n2) ? n2 : 0.f);  // clamp_min(0), NaN kept
+  return __fsqrt_rn(n2);
+}
+
+template <typename TO>
+__global__ void norm_finalize_kernel(const float* __restrict__ wpart, int nw, const float* __restrict__ cpart,
+                                     int nc, const float* __restrict__ bpart, int nb, int64_t M, float two_s,
+                                     float s2, bool scale_zero, TO* __restrict__ norm_out,
+                                     float* __restrict__ parts) {
+  const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  float w = 0.f, c = 0.f, b = 0.f;
+  for (int i = 0; i < nw; ++i) w += wpart[int64_t(i) * M + m];
+  for (int i = 0; i < nc; ++i) c += cpart[int64_t(i) * M + m];
+  for (int i = 0; i < nb; ++i) b += bpart[int64_t(i) * M + m];
+  float n;
+  if (scale_zero) {
+    const float x = (w > 0.f) ? w : ((w != w) ? w : 0.f);
+    n = __fsqrt_rn(x);
+  } else {
+    n = assemble_one(w, c, b, two_s, s2);
+  }
+  norm_out[m] = from_f32<TO>(n);
+  if (parts) {
+    parts[m] = w;
+    parts[M + m] = c;
+    parts[2 * M + m] = b;
+  }
+}
+
+// get_weight_norm (dora.py:1012-1022): one warp per row.
+template <typename TW, typename TL>
+__global__ void dense_norm_kernel(const TW* __restrict__ W, const TL* __restrict__ L, float s, int64_t M, int64_t K,
+                                  TW* __restrict__ out) {
+  const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float acc = 0.f;
+  for (int64_t k = lane; k < K; k += 32) {
+    const float t = __fadd_rn(to_f32(W[row * K + k]), __fmul_rn(s, to_f32(L[row * K + k])));
+    acc = fmaf(t, t, acc);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) out[row] = from_f32<TW>(__fsqrt_rn(acc));
+}
+
+template <typename TW>
+static void launch_dense_norm(int ld, const void* W, const void* L, float s, int64_t M, int64_t K, void* out,
+                              cudaStream_t st) {
+  const unsigned grid = unsigned((M + 7) / 8);
+  auto w = static_cast<const TW*>(W);
+  auto o = static_cast<TW*>(out);
+  switch (ld) {
+    case DORA_DTYPE_BF16: dense_norm_kernel<<<grid, 256, 0, st>>>(w, static_cast<const __nv_bfloat16*>(L), s, M, K, o); break;
+    case DORA_DTYPE_F16: dense_norm_kernel<<<grid, 256, 0, st>>>(w, static_cast<const __half*>(L), s, M, K, o); break;
+    default: dense_norm_kernel<<<grid, 256, 0, st>>>(w, static_cast<const float*>(L), s, M, K, o); break;
+  }
+}
+
+__global__ void assembly_kernel(const float* __restrict__ w, const float* __restrict__ c, const float* __restrict__ b,
+                                float two_s, float s2, float* __restrict__ out, int64_t n) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = assemble_one(w[i], c[i], b[i], two_s, s2);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+template <typename TX, typename TY, typename TZ, int MODE, bool SSQ>
+static void launch_simt(const void* X, int64_t ldx, const void* Y, int64_t ldy, const void* Z, int64_t ldz, int64_t M,
+                        int64_t N, int64_t K, int ksplit, float* rowdot, float* ssq, float* C, int64_t ldc,
+                        cudaStream_t st) {
+  const int64_t kchunk = ((K + ksplit - 1) / ksplit + 15) / 16 * 16;
+  dim3 grid(unsigned((N + 63) / 64), unsigned((M + 63) / 64), unsigned(ksplit));
+  simt_rowdot_gemm<TX, TY, TZ, MODE, SSQ><<<grid, 256, 0, st>>>(
+      static_cast<const TX*>(X), ldx, static_cast<const TY*>(Y), ldy, static_cast<const TZ*>(Z), ldz, M, N, K,
+      kchunk, rowdot, ssq, C, ldc);
+}
+
+// Dispatch on three runtime dtypes.
+template <int MODE, bool SSQ, typename TX, typename TY>
+static void simt_z(int dz, const void* X, int64_t ldx, const void* Y, int64_t ldy, const void* Z, int64_t ldz,
+                   int64_t M, int64_t N, int64_t K, int ks, float* rd, float* ss, float* C, int64_t ldc,
+                   cudaStream_t st) {
+  switch (dz) {
+    case DORA_DTYPE_BF16: launch_simt<TX, TY, __nv_bfloat16, MODE, SSQ>(X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+    case DORA_DTYPE_F16: launch_simt<TX, TY, __half, MODE, SSQ>(X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+    default: launch_simt<TX, TY, float, MODE, SSQ>(X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+  }
+}
+template <int MODE, bool SSQ, typename TX>
+static void simt_y(int dy, int dz, const void* X, int64_t ldx, const void* Y, int64_t ldy, const void* Z, int64_t ldz,
+                   int64_t M, int64_t N, int64_t K, int ks, float* rd, float* ss, float* C, int64_t ldc,
+                   cudaStream_t st) {
+  switch (dy) {
+    case DORA_DTYPE_BF16: simt_z<MODE, SSQ, TX, __nv_bfloat16>(dz, X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+    case DORA_DTYPE_F16: simt_z<MODE, SSQ, TX, __half>(dz, X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+    default: simt_z<MODE, SSQ, TX, float>(dz, X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+  }
+}
+template <int MODE, bool SSQ>
+void simt_gemm(int dx, int dy, int dz, const void* X, int64_t ldx, const void* Y, int64_t ldy, const void* Z,
+               int64_t ldz, int64_t M, int64_t N, int64_t K, int ks, float* rd, float* ss, float* C, int64_t ldc,
+               cudaStream_t st) {
+  switch (dx) {
+    case DORA_DTYPE_BF16: simt_y<MODE, SSQ, __nv_bfloat16>(dy, dz, X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+    case DORA_DTYPE_F16: simt_y<MODE, SSQ, __half>(dy, dz, X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+    default: simt_y<MODE, SSQ, float>(dy, dz, X, ldx, Y, ldy, Z, ldz, M, N, K, ks, rd, ss, C, ldc, st); break;
+  }
+}
+template void simt_gemm<kGemmRowdot, true>(int, int, int, const void*, int64_t, const void*, int64_t, const void*,
+                                           int64_t, int64_t, int64_t, int64_t, int, float*, float*, float*, int64_t,
+                                           cudaStream_t);
+template void simt_gemm<kGemmRowdot, false>(int, int, int, const void*, int64_t, const void*, int64_t, const void*,
+                                            int64_t, int64_t, int64_t, int64_t, int, float*, float*, float*, int64_t,
+                                            cudaStream_t);
+template void simt_gemm<kGemmStore, false>(int, int, int, const void*, int64_t, const void*, int64_t, const void*,
+                                           int64_t, int64_t, int64_t, int64_t, int, float*, float*, float*, int64_t,
+                                           cudaStream_t);
+
+void launch_row_sumsq(int dx, const void* X, int64_t M, int64_t K, float* out, cudaStream_t st) {
+  const unsigned grid = unsigned((M + 7) / 8);
+  switch (dx) {
+    case DORA_DTYPE_BF16: row_sumsq_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(X), M, K, out); break;
+    case DORA_DTYPE_F16: row_sumsq_kernel<<<grid, 256, 0, st>>>(static_cast<const __half*>(X), M, K, out); break;
+    default: row_sumsq_kernel<<<grid, 256, 0, st>>>(static_cast<const float*>(X), M, K, out); break;
+  }
+}
+
+void launch_gram_reduce(const float* part, int nsplit, int64_t r, float* yt, int half_dtype, void* hi, void* lo,
+                        cudaStream_t st) {
+  const unsigned grid = unsigned((r * r + 255) / 256);
+  if (half_dtype == DORA_DTYPE_F16)
+    gram_reduce_kernel<__half><<<grid, 256, 0, st>>>(part, nsplit, r, yt, static_cast<__half*>(hi), static_cast<__half*>(lo));
+  else
+    gram_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(part, nsplit, r, yt, static_cast<__nv_bfloat16*>(hi),
+                                                            static_cast<__nv_bfloat16*>(lo));
+}
+
+void launch_norm_finalize(const float* wpart, int nw, const float* cpart, int nc, const float* bpart, int nb,
+                          int64_t M, double scale, int out_dtype, void* norm_out, float* parts, cudaStream_t st) {
+  const float two_s = float(2.0 * scale), s2 = float(scale * scale);
+  const bool sz = (scale == 0.0);
+  const unsigned grid = unsigned((M + 255) / 256);
+  switch (out_dtype) {
+    case DORA_DTYPE_BF16:
+      norm_finalize_kernel<<<grid, 256, 0, st>>>(wpart, nw, cpart, nc, bpart, nb, M, two_s, s2, sz,
+                                                 static_cast<__nv_bfloat16*>(norm_out), parts);
+      break;
+    case DORA_DTYPE_F16:
+      norm_finalize_kernel<<<grid, 256, 0, st>>>(wpart, nw, cpart, nc, bpart, nb, M, two_s, s2, sz,
+                                                 static_cast<__half*>(norm_out), parts);
+      break;
+    default:
+      norm_finalize_kernel<<<grid, 256, 0, st>>>(wpart, nw, cpart, nc, bpart, nb, M, two_s, s2, sz,
+                                                 static_cast<float*>(norm_out), parts);
+      break;
+  }
+}
+
+}  // namespace dora
+
+using namespace dora;
+
+extern "C" int dora_norm_assembly(const float* w_norm_sq, const float* cross, const float* ba, double scale,
+                                  float* norm_out, int64_t n, void* stream) {
+  if (n < 0) return DORA_ERR_INVALID_ARGUMENT;
+  if (n == 0) return DORA_OK;
+  if (!w_norm_sq || !cross || !ba || !norm_out) return DORA_ERR_INVALID_ARGUMENT;
+  // Coefficients formed in double and rounded to fp32, like PyTorch's
+  // Python-scalar promotion (dora_fused.py:970-975).
+  const float two_s = float(2.0 * scale), s2 = float(scale * scale);
+  assembly_kernel<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(w_norm_sq, cross, ba,
+                                                                                            two_s, s2, norm_out, n);
+  return check_launch();
+}
+
+extern "C" int dora_weight_norm_dense(const void* W, const void* L, int64_t out_features, int64_t in_features,
+                                      int w_dtype, int l_dtype, double scale, void* norm_out, void* stream) {
+  if (out_features < 0 || in_features < 0 || !dtype_ok(w_dtype) || !dtype_ok(l_dtype)) return DORA_ERR_INVALID_ARGUMENT;
+  if (out_features == 0) return DORA_OK;
+  if (!norm_out || (in_features > 0 && (!W || !L))) return DORA_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float s = float(scale);
+  switch (w_dtype) {
+    case DORA_DTYPE_BF16: launch_dense_norm<__nv_bfloat16>(l_dtype, W, L, s, out_features, in_features, norm_out, st); break;
+    case DORA_DTYPE_F16: launch_dense_norm<__half>(l_dtype, W, L, s, out_features, in_features, norm_out, st); break;
+    default: launch_dense_norm<float>(l_dtype, W, L, s, out_features, in_features, norm_out, st); break;
+  }
+  return check_launch();
+}

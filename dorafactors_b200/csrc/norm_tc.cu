@@ -1,0 +1,443 @@
+// Tensor-core (tcgen05 + TMEM + TMA) row-dot GEMM for the factored DoRA norm.
+//
+// One CTA computes a 128 x NT tile of C = X Y^T over a contiguous range of
+// K, with the accumulator in tensor memory:
+//   warp 0      TMA producer: 128-byte-swizzled X [128 x 64] and Y [NT x 64]
+//               tiles into a multi-stage shared-memory ring (mbarrier
+//               complete_tx signalling);
+//   warp 1      owns the TMEM allocation and issues tcgen05.mma (kind::f16,
+//               fp32 accumulate) from one thread, 4 x (NT / <=256) MMAs per
+//               k-block, releasing each ring slot with tcgen05.commit;
+//   warps 2..5  one thread per tile row (= TMEM lane).  While the mainloop
+//               runs they add up the squares of their row of X straight from
+//               the staged X tiles (||W0||^2 costs no extra HBM traffic).
+//               After the last MMA they read the accumulator row with
+//               tcgen05.ld and either contract it with Z (rowsum(C * Z), the
+//               factored norm's cross / B G B^T terms) or store it (Gram
+//               partials).
+// Every mbarrier wait is bounded (about one second); on expiry the kernel
+// records DORA_ERR_DEVICE_TIMEOUT in the device error word, drains what it
+// issued and returns instead of hanging.  No cluster, no multicast.
+#include <mutex>
+#include <type_traits>
+
+#include "norm_internal.cuh"
+
+namespace dora {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 half-precision elements = one 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr uint32_t kXTileBytes = BM * BK * 2;
+constexpr long long kWaitCycles = 1ll << 31;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase of the given parity to complete, for at most ~2^31 cycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      record_device_error(DORA_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major tile stored as 128-byte rows
+// in the 128-byte swizzle pattern (the layout TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B): 8-row core groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFFu);   // start address
+  d |= uint64_t(1) << 16;                  // leading byte offset (unused when swizzled)
+  d |= uint64_t(1024 >> 4) << 32;          // stride byte offset: 8 rows x 128 B
+  d |= uint64_t(1) << 46;                  // descriptor version for sm_100
+  d |= uint64_t(2) << 61;                  // swizzle mode: 128 B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, A/B both bf16 or both
+// f16, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, int n) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | (uint32_t(n >> 3) << 17) |
+         (uint32_t(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct SmemLayout {
+  uint32_t stage_bytes;
+  uint32_t bar_offset;  // from the 1024-aligned base
+  uint32_t total;       // dynamic shared memory to request (includes alignment slack)
+};
+__host__ __device__ inline SmemLayout smem_layout(int nt, int stages) {
+  SmemLayout L;
+  L.stage_bytes = kXTileBytes + uint32_t(nt) * 128u;
+  L.bar_offset = L.stage_bytes * uint32_t(stages);
+  L.total = 1024u + L.bar_offset + 256u;
+  return L;
+}
+
+template <typename T, int MODE, bool kSumSq>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY1,
+                 const __grid_constant__ CUtensorMap tmY2, int two_y, const T* __restrict__ Z, int64_t ldz,
+                 int64_t M, int64_t N, int nt, int ybox, int n_tiles, int m_tiles, int kblocks, int k_splits,
+                 int stages, uint32_t tmem_cols, float* __restrict__ rowdot_part, float* __restrict__ sumsq_part,
+                 float* __restrict__ C) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const SmemLayout L = smem_layout(nt, stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bar_offset);
+  uint64_t* empty = full + stages;
+  uint64_t* done = empty + stages;
+  uint64_t* drain = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* aborted = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int unit = blockIdx.x;
+  const int m_tile = unit % m_tiles;
+  const int rest = unit / m_tiles;
+  const int n_tile = rest % n_tiles;
+  const int ks = rest / n_tiles;
+  const int64_t m0 = int64_t(m_tile) * BM;
+  const int64_t n0 = int64_t(n_tile) * nt;
+  const int kb_total = two_y ? 2 * kblocks : kblocks;
+  const int kb0 = int(int64_t(ks) * kb_total / k_splits);
+  const int kb1 = int(int64_t(ks + 1) * kb_total / k_splits);
+  const int iters = kb1 - kb0;
+  const bool do_ssq = kSumSq && n_tile == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + (do_ssq ? 4 : 0));
+    }
+    mbar_init(done, 1);
+    mbar_init(drain, 1);
+    *aborted = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tx_bytes = L.stage_bytes;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmY1)) : "memory");
+      int issued = 0;
+      for (int it = 0; it < iters; ++it) {
+        const int s = it % stages, round = it / stages;
+        if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) { *aborted = 1; break; }
+        if (*aborted) break;
+        const int kb = kb0 + it;
+        const bool second = kb >= kblocks;
+        const int kx = (second ? kb - kblocks : kb) * BK;
+        uint8_t* sX = base + size_t(s) * L.stage_bytes;
+        uint8_t* sY = sX + kXTileBytes;
+        mbar_expect_tx(&full[s], tx_bytes);
+        tma_load_2d(sX, &tmX, &full[s], kx, int(m0));
+        const CUtensorMap* ym = second ? &tmY2 : &tmY1;
+        for (int j = 0; j * ybox < nt; ++j) tma_load_2d(sY + size_t(j) * ybox * 128, ym, &full[s], kx, int(n0) + j * ybox);
+        issued = it + 1;
+      }
+      if (*aborted) {
+        // Let every load this thread issued land before the CTA's shared memory is released.
+        for (int it = issued - stages > 0 ? issued - stages : 0; it < issued; ++it)
+          mbar_wait(&full[it % stages], (it / stages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+      int it = 0;
+      for (; it < iters; ++it) {
+        const int s = it % stages, round = it / stages;
+        if (!mbar_wait(&full[s], round & 1)) { *aborted = 1; break; }
+        tc_fence_after();
+        const uint32_t sX = smem_u32(base + size_t(s) * L.stage_bytes);
+        const uint32_t sY = sX + kXTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t adesc = sw128_desc(sX + kk * 32);
+          for (int c0 = 0; c0 < nt; c0 += 256) {
+            const int n = (nt - c0) < 256 ? (nt - c0) : 256;
+            const uint64_t bdesc = sw128_desc(sY + uint32_t(c0) * 128u + kk * 32);
+            umma_f16(tmem_base + uint32_t(c0), adesc, bdesc, make_idesc(bf16, n), (it > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(&empty[s]);
+      }
+      if (*aborted) {
+        umma_commit(drain);  // completes once every MMA issued above has finished
+        mbar_wait(drain, 0);
+      } else {
+        umma_commit(done);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ row threads
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int64_t m = m0 + row;
+    float ssq = 0.f;
+    if (do_ssq) {
+      for (int it = 0; it < iters; ++it) {
+        const int s = it % stages, round = it / stages;
+        if (!mbar_wait(&full[s], round & 1)) { *aborted = 1; break; }
+        const uint8_t* rowp = base + size_t(s) * L.stage_bytes + row * 128;
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          // Rotate the 16-byte chunk order by lane so a quarter-warp touches 8 distinct bank groups.
+          const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((p + lane) & 7) * 16);
+          const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float x = to_f32(h[e]);
+            ssq = fmaf(x, x, ssq);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+    }
+    const bool ok = !*aborted && mbar_wait(done, 0);
+    if (ok) {
+      tc_fence_after();
+      const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16);
+      float acc = 0.f;
+      for (int c0 = 0; c0 < nt; c0 += 32) {
+        if (n0 + c0 >= N) break;
+        float v[32];
+        tmem_ld32(trow + uint32_t(c0), v);
+        if (m < M) {
+          const int64_t nbase = n0 + c0;
+          const int cnt = (N - nbase) < 32 ? int(N - nbase) : 32;
+          if constexpr (MODE == kGemmRowdot) {
+            const T* zr = Z + m * ldz + nbase;
+            if (cnt == 32 && ((reinterpret_cast<uintptr_t>(zr) & 15u) == 0)) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 zv = __ldg(reinterpret_cast<const uint4*>(zr) + j);
+                const T* zh = reinterpret_cast<const T*>(&zv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc = fmaf(v[j * 8 + e], to_f32(zh[e]), acc);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < cnt) acc = fmaf(v[j], to_f32(zr[j]), acc);
+            }
+          } else {
+            float* cr = C + (int64_t(ks) * M + m) * N + nbase;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < cnt) cr[j] = v[j];
+          }
+        }
+      }
+      if (m < M) {
+        if constexpr (MODE == kGemmRowdot) rowdot_part[(int64_t(ks) * n_tiles + n_tile) * M + m] = acc;
+        if (do_ssq) sumsq_part[int64_t(ks) * M + m] = ssq;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major map over a row-major [rows x k] half-precision matrix, box
+// [box_rows x 64], 128-byte swizzle, zero fill outside the matrix.
+static bool make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t rows, int64_t k, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(k) * 2};
+  cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapDataType dt = dtype == DORA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static int stages_for(int nt) {
+  const uint32_t stage = kXTileBytes + uint32_t(nt) * 128u;
+  int s = int((220u * 1024u) / stage);
+  if (s > 8) s = 8;
+  return s;
+}
+
+}  // namespace tc
+
+TcGemmShape tc_gemm_shape(int64_t M, int64_t N, int64_t K) {
+  TcGemmShape s;
+  if (N <= 256) {
+    s.nt = int((N + 15) / 16 * 16);
+    s.n_tiles = 1;
+  } else if (N <= 512) {
+    s.nt = int((N + 127) / 128 * 128);
+    s.n_tiles = 1;
+  } else {
+    s.nt = 256;
+    s.n_tiles = int((N + 255) / 256);
+  }
+  s.m_tiles = int((M + tc::BM - 1) / tc::BM);
+  s.kblocks = int((K + tc::BK - 1) / tc::BK);
+  return s;
+}
+
+bool tc_gemm_supported(int dtype, int64_t M, int64_t N, int64_t K, const void* X, const void* Y, const void* Z,
+                       int64_t ldz) {
+  if (dtype != DORA_DTYPE_BF16 && dtype != DORA_DTYPE_F16) return false;
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if (K % 8 != 0) return false;  // TMA row stride must be a multiple of 16 bytes
+  if (M > (int64_t(1) << 31) - 1 || N > (int64_t(1) << 31) - 1 || K > (int64_t(1) << 31) - 1) return false;
+  if (!aligned16(X) || !aligned16(Y)) return false;
+  (void)Z;
+  (void)ldz;
+  return true;
+}
+
+template <typename T, int MODE, bool SSQ>
+static int launch_tc(const TcGemmArgs& a, const TcGemmShape& sh, const CUtensorMap& mx, const CUtensorMap& my1,
+                     const CUtensorMap& my2, int ybox, int stages, cudaStream_t st) {
+  const tc::SmemLayout L = tc::smem_layout(sh.nt, stages);
+  auto kfn = tc::tc_rowdot_kernel<T, MODE, SSQ>;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
+  if (e != cudaSuccess) return set_cuda_error(e);
+  uint32_t cols = 32;
+  while (cols < uint32_t(sh.nt)) cols <<= 1;
+  const unsigned grid = unsigned(sh.m_tiles) * unsigned(sh.n_tiles) * unsigned(a.k_splits);
+  kfn<<<grid, tc::kThreads, L.total, st>>>(mx, my1, my2, a.Y2 ? 1 : 0, static_cast<const T*>(a.Z), a.ldz, a.M, a.N,
+                                            sh.nt, ybox, sh.n_tiles, sh.m_tiles, sh.kblocks, a.k_splits, stages, cols,
+                                            a.rowdot_part, a.sumsq_part, a.C);
+  return check_launch();
+}
+
+template <typename T>
+static int dispatch_tc(const TcGemmArgs& a, const TcGemmShape& sh, const CUtensorMap& mx, const CUtensorMap& my1,
+                       const CUtensorMap& my2, int ybox, int stages, cudaStream_t st) {
+  if (a.mode == kGemmStore) return launch_tc<T, kGemmStore, false>(a, sh, mx, my1, my2, ybox, stages, st);
+  if (a.sumsq) return launch_tc<T, kGemmRowdot, true>(a, sh, mx, my1, my2, ybox, stages, st);
+  return launch_tc<T, kGemmRowdot, false>(a, sh, mx, my1, my2, ybox, stages, st);
+}
+
+int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st) {
+  const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K);
+  const int kb_total = a.Y2 ? 2 * sh.kblocks : sh.kblocks;
+  if (a.k_splits < 1 || a.k_splits > kb_total) return DORA_ERR_INVALID_ARGUMENT;
+  const int ybox = sh.nt <= 256 ? sh.nt : 128;
+  CUtensorMap mx, my1, my2;
+  if (!tc::make_map(&mx, a.X, a.dtype, a.M, a.K, tc::BM) || !tc::make_map(&my1, a.Y1, a.dtype, a.N, a.K, ybox) ||
+      !tc::make_map(&my2, a.Y2 ? a.Y2 : a.Y1, a.dtype, a.N, a.K, ybox))
+    return DORA_ERR_CUDA;
+  const int stages = tc::stages_for(sh.nt);
+  if (a.dtype == DORA_DTYPE_BF16) return dispatch_tc<__nv_bfloat16>(a, sh, mx, my1, my2, ybox, stages, st);
+  return dispatch_tc<__half>(a, sh, mx, my1, my2, ybox, stages, st);
+}
+
+}  // namespace dora

@@ -1,0 +1,67 @@
+"""A self-contained DoRA linear layer wired the way PEFT wires it.
+
+``DoraLinear`` stands in for ``peft.tuners.lora.layer.Linear`` with
+``use_dora=True`` (layer.py:653-878) plus ``DoraLinearVariant.forward``
+(variants.py:214-284): a frozen base ``nn.Linear``, ``lora_A`` / ``lora_B``
+adapters, and the magnitude module ``DoraLinearLayer`` that returns the DoRA
+delta.  It exists so the hot path can be exercised and benchmarked without the
+rest of PEFT; inside PEFT the same ``DoraLinearLayer`` is driven by PEFT's own
+variant code.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+from torch import nn
+
+from .dora import DoraLinearLayer
+
+
+class DoraLinear(nn.Module):
+    """y = base(x) + DoRA delta.  ``scaling`` is lora_alpha / r (layer.py:254-257)."""
+
+    def __init__(self, base_layer: nn.Linear, r: int, scaling: float, dropout: float = 0.0,
+                 init_lora_B_zero: bool = True):
+        super().__init__()
+        self.base_layer = base_layer
+        self.base_layer.weight.requires_grad_(False)
+        if self.base_layer.bias is not None:
+            self.base_layer.bias.requires_grad_(False)
+        w = base_layer.weight
+        self.lora_A = nn.Linear(base_layer.in_features, r, bias=False, device=w.device, dtype=w.dtype)
+        self.lora_B = nn.Linear(r, base_layer.out_features, bias=False, device=w.device, dtype=w.dtype)
+        nn.init.kaiming_uniform_(self.lora_A.weight, a=math.sqrt(5))
+        if init_lora_B_zero:
+            nn.init.zeros_(self.lora_B.weight)
+        self.scaling = float(scaling)
+        self.lora_dropout = nn.Dropout(dropout) if dropout > 0 else nn.Identity()
+        self.lora_magnitude_vector = DoraLinearLayer(fan_in_fan_out=False)
+        self.reset_magnitude()
+
+    @torch.no_grad()
+    def reset_magnitude(self) -> None:
+        """m = ||W0 + s B A|| per output row (DoraLinearVariant.init, variants.py:133-161)."""
+        self.lora_magnitude_vector.update_layer(
+            base_layer=self.base_layer, lora_A=self.lora_A.weight, lora_B=self.lora_B.weight, scaling=self.scaling
+        )
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        result = self.base_layer(x)
+        if isinstance(self.lora_dropout, nn.Identity) or not self.training:
+            base_result = result
+            xd = x
+        else:
+            xd = self.lora_dropout(x)
+            base_result = None
+        delta = self.lora_magnitude_vector(
+            xd, lora_A=self.lora_A, lora_B=self.lora_B, scaling=self.scaling, base_layer=self.base_layer,
+            base_result=base_result,
+        )
+        if delta.dtype != result.dtype:
+            delta = delta.to(result.dtype)
+        delta_depends_on_result = base_result is result and self.base_layer.bias is None
+        if delta_depends_on_result and torch.is_grad_enabled():
+            return result + delta
+        return result.add_(delta)

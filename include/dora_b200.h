@@ -1,0 +1,159 @@
+/*
+ * dora_b200.h -- C ABI of the B200-native DoRA hot path.
+ *
+ * One shared library, libdora_b200.so, built for sm_100a.  Every entry point
+ * takes plain device pointers, sizes, dtype codes and a CUDA stream handle
+ * (a cudaStream_t passed as void*; NULL is the legacy default stream), queues
+ * its kernels on that stream and returns a dora_status_t without waiting for
+ * them.  No entry point allocates device memory: scratch space is passed in
+ * by the caller, sized by the matching *_workspace_size query.
+ *
+ * Each entry point names the reference interface it replaces, as
+ * file:line inside sockeye44/dorafactors, where "dora.py" and "dora_fused.py"
+ * are code/peft_patched/src/peft/tuners/lora/{dora,dora_fused}.py.
+ *
+ * Layout conventions.  Activations are row-major [rows x cols] (cols = the
+ * layer's out_features, rows = every leading dim flattened), contiguous.  The
+ * per-column scale g ("mag_norm_scale") is a contiguous vector of cols
+ * elements.  Weights are row-major and contiguous: W0 [out x in], A [r x in],
+ * B [out x r].
+ */
+#ifndef DORA_B200_H_
+#define DORA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types.  Values are part of the ABI. */
+typedef enum {
+  DORA_DTYPE_F32 = 0,
+  DORA_DTYPE_F16 = 1,
+  DORA_DTYPE_BF16 = 2
+} dora_dtype_t;
+
+/* Status codes.  Values are part of the ABI. */
+typedef enum {
+  DORA_OK = 0,
+  DORA_ERR_INVALID_ARGUMENT = 1, /* bad size, dtype, null pointer or alias */
+  DORA_ERR_UNSUPPORTED = 2,      /* valid request this build cannot serve */
+  DORA_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  DORA_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed */
+  DORA_ERR_DEVICE_TIMEOUT = 5    /* a bounded device-side wait gave up */
+} dora_status_t;
+
+/* Library version as 10000*major + 100*minor + patch. */
+int dora_version(void);
+
+/* Human-readable text of a status code (static storage). */
+const char* dora_status_string(int status);
+
+/* Text of the last CUDA error seen by this thread inside the library. */
+const char* dora_last_cuda_error(void);
+
+/* Number of kernels this library has launched in this process (all devices). */
+unsigned long long dora_launch_count(void);
+
+/*
+ * Device-side error word of the current device: 0 when no kernel has
+ * recorded a failure, else a DORA_ERR_* code set by a kernel whose bounded
+ * wait expired.  Synchronises the current device.  With reset != 0 the word
+ * is cleared after reading.  Returns DORA_ERR_CUDA if the read itself fails
+ * (*out untouched).
+ */
+int dora_device_error(int reset, int* out);
+
+/*
+ * Fused compose forward.
+ *   out[i,j]   = (g[j] - 1) * base[i,j] + g[j] * (scale * lora[i,j])
+ *   inner[i,j] = scale * lora[i,j] + base[i,j]            (only if inner != NULL)
+ * Arithmetic in fp32, one rounding into act_dtype per output.  out may alias
+ * lora (in-place compose); inner must not alias any input.  g_dtype is
+ * act_dtype or DORA_DTYPE_F32 (fp32 magnitude with half activations).
+ * rows * cols == 0 is a no-op.
+ *
+ * Replaces fused_dora_compose (dora_fused.py:539-671, kernels 367-459) and
+ * fused_dora_forward_and_inner (dora_fused.py:674-772, kernel 461-514).
+ */
+int dora_compose_fwd(const void* lora, const void* base, const void* g, int g_dtype, double scale,
+                     void* out, void* inner, int64_t rows, int64_t cols, int act_dtype, void* stream);
+
+/*
+ * Bytes of workspace dora_compose_bwd needs to produce d_g for this shape on
+ * the current device (0 for an empty tensor).  The workspace must be 256-byte
+ * aligned.  It starts with a region of completion counters that must be zero
+ * before the first call; every successful call leaves them zero again, so a
+ * zero-filled workspace may be reused by later calls on the same stream
+ * without clearing.  Calls that overlap on the GPU need separate workspaces.
+ */
+size_t dora_compose_bwd_workspace_size(int64_t rows, int64_t cols, int act_dtype);
+
+/*
+ * Fused compose backward, one pass over d_out (and inner):
+ *   d_lora[i,j] = (g[j] * scale) * d_out[i,j]             (if d_lora != NULL)
+ *   d_base[i,j] = (g[j] - 1) * d_out[i,j]                 (if d_base != NULL)
+ *   d_g[j]      = sum_i inner[i,j] * d_out[i,j]           (if d_g != NULL)
+ * d_lora / d_base are in act_dtype, d_g in g_dtype.  The column sum runs in
+ * fp32 in a fixed order (per-thread, then CTA tree, then per-CTA partials
+ * folded by the last CTA of each column tile), so results are deterministic.
+ * inner is required iff d_g != NULL.
+ *
+ * Replaces FusedDoRAComposeFunction.backward / _fused_backward_triton
+ * (dora_fused.py:1137-1206, 1264-1344, kernel 1010-1062), including the
+ * PyTorch d_mag reduction of dora_fused.py:1330-1342.
+ */
+int dora_compose_bwd(const void* d_out, const void* inner, const void* g, int g_dtype, double scale,
+                     void* d_lora, void* d_base, void* d_g, void* workspace, size_t workspace_bytes,
+                     int64_t rows, int64_t cols, int act_dtype, void* stream);
+
+/*
+ * Norm assembly: norm[i] = sqrt(max(w[i] + (2s)*c[i] + (s*s)*b[i], 0)) in
+ * fp32, four separately rounded ops in that order, NaN kept by the clamp,
+ * IEEE square root.
+ *
+ * Replaces fused_norm_assembly (dora_fused.py:873-988, kernel 789-861).
+ */
+int dora_norm_assembly(const float* w_norm_sq, const float* cross, const float* ba, double scale,
+                       float* norm_out, int64_t n, void* stream);
+
+/* Bytes of workspace dora_weight_norm needs for this problem. */
+size_t dora_weight_norm_workspace_size(int64_t out_features, int64_t in_features, int64_t rank,
+                                       int w_dtype, int a_dtype, int b_dtype);
+
+/*
+ * Factored row norm of W0 + scale * B @ A without forming B @ A:
+ *   norm[j]^2 = ||W0[j,:]||^2 + 2 s <B[j,:], (W0 A^T)[j,:]> + s^2 B[j,:] (A A^T) B[j,:]^T
+ * then the assembly of dora_norm_assembly and a cast to w_dtype (norm_out has
+ * w_dtype).  When parts != NULL it receives 3*out floats: ||W0||^2, the cross
+ * term and the B G B^T term, each [out] in fp32.  scale == 0 computes
+ * sqrt(||W0||^2) only.  bf16 and fp16 weights with adapters of the same dtype
+ * run on the tcgen05 tensor cores; every other dtype mix runs an fp32 CUDA-core
+ * path.
+ *
+ * Replaces DoraLinearLayer._get_weight_norm_linear (dora.py:1024-1153) with
+ * its fused_norm_assembly call (dora.py:1136-1148).
+ */
+int dora_weight_norm(const void* W, const void* A, const void* B, int64_t out_features,
+                     int64_t in_features, int64_t rank, int w_dtype, int a_dtype, int b_dtype,
+                     double scale, void* norm_out, float* parts, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/*
+ * Dense row norm: norm[j] = || W[j,:] + scale * L[j,:] || in fp32 (scale * L
+ * rounded first, then the sum, then a fp32 sum of squares and an IEEE square
+ * root), cast to w_dtype.  L is the dense [out x in] LoRA weight.
+ *
+ * Replaces DoraLinearLayer.get_weight_norm (dora.py:1012-1022), which the
+ * merge / unmerge paths use (variants.py:164-212).
+ */
+int dora_weight_norm_dense(const void* W, const void* L, int64_t out_features, int64_t in_features, int w_dtype,
+                           int l_dtype, double scale, void* norm_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DORA_B200_H_ */

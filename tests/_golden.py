@@ -67,3 +67,23 @@ def rel_errors(a, ref) -> tuple[float, float]:
 def assert_close(a, ref, rtol: float, what: str = "") -> None:
     l2, linf = rel_errors(a, ref)
     assert l2 <= rtol and linf <= rtol, f"{what}: rel-L2 {l2:.3e}, rel-max {linf:.3e} > {rtol:.1e}"
+
+
+# ---------------------------------------------------------------------------
+# numpy <-> torch for the GPU tests
+# ---------------------------------------------------------------------------
+def torch_dtype(name: str):
+    import torch
+
+    return {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[name]
+
+
+def to_dev(arr, dtype: str, device="cuda"):
+    """float32 array holding dtype-representable values -> torch tensor of that dtype (exact)."""
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(arr, dtype=np.float32)).to(device).to(torch_dtype(dtype))
+
+
+def to_np(t) -> np.ndarray:
+    return t.detach().float().cpu().numpy()

@@ -1,0 +1,127 @@
+"""The whole adapted linear (base + LoRA + DoRA) on the native path: forward and
+backward against the reference's golden fixtures and the oracle.
+
+Tolerance: 1e-2 relative (normwise) in bf16, 1e-5 in fp32, for y, the delta,
+the norm and the gradients dx, dA, dB, dm.  The base and LoRA GEMMs are
+PyTorch/cuBLAS (owned by the caller, as in PEFT); on fp32 they run with TF32
+disabled.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from _golden import RTOL, assert_close, load_group, to_dev, to_np
+from oracle import dora_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+LAYER = load_group("layer")
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32_no_device_error():
+    from dorafactors_b200 import _native
+
+    old = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+    assert _native.device_error(reset=True) == 0
+
+
+def _build(st, dt):
+    from dorafactors_b200.dora import DoraLinearLayer
+
+    W = to_dev(st["W"], dt)
+    out_f, in_f = W.shape
+    r = st["A"].shape[0]
+    base = torch.nn.Linear(in_f, out_f, bias="bias" in st, device="cuda", dtype=W.dtype)
+    lora_A = torch.nn.Linear(in_f, r, bias=False, device="cuda", dtype=W.dtype)
+    lora_B = torch.nn.Linear(r, out_f, bias=False, device="cuda", dtype=W.dtype)
+    with torch.no_grad():
+        base.weight.copy_(W)
+        if "bias" in st:
+            base.bias.copy_(to_dev(st["bias"], dt))
+        lora_A.weight.copy_(to_dev(st["A"], dt))
+        lora_B.weight.copy_(to_dev(st["B"], dt))
+    base.requires_grad_(False)
+    layer = DoraLinearLayer(fan_in_fan_out=False)
+    layer.update_layer(base_layer=base, lora_A=lora_A.weight, lora_B=lora_B.weight, scaling=float(st["scale"]))
+    return base, lora_A, lora_B, layer
+
+
+@pytest.mark.parametrize("case", sorted(LAYER))
+def test_layer_golden(case):
+    st = LAYER[case]
+    dt = st["dtype"]
+    base, lora_A, lora_B, layer = _build(st, dt)
+    assert_close(to_np(layer.weight), st["m"], RTOL[dt], "initial magnitude")
+    x = to_dev(st["x"], dt).requires_grad_(True)
+    result = base(x)
+    delta = layer(x, lora_A=lora_A, lora_B=lora_B, scaling=float(st["scale"]), base_layer=base, base_result=result)
+    y = result + delta
+    y.backward(to_dev(st["dy"], dt))
+    got = {"y": y, "delta": delta, "dx": x.grad, "dA": lora_A.weight.grad, "dB": lora_B.weight.grad,
+           "dm": layer.weight.grad}
+    for k, v in got.items():
+        assert_close(to_np(v), st[k], RTOL[dt], f"{case} {k}")
+
+
+@pytest.mark.parametrize("dtype,T,in_f,out_f,r", [("bf16", 256, 512, 768, 32), ("fp32", 64, 256, 320, 16),
+                                                  ("bf16", 2048, 4096, 4096, 16)])
+def test_dora_linear_vs_oracle(dtype, T, in_f, out_f, r):
+    """DoraLinear (PEFT wiring) forward + backward against the oracle's eager restatement."""
+    from dorafactors_b200.layer import DoraLinear
+
+    rng = np.random.default_rng(T + in_f + r)
+    W = orc.round_to(rng.standard_normal((out_f, in_f)) * 0.02, dtype)
+    A = orc.round_to(rng.uniform(-1, 1, (r, in_f)) / np.sqrt(in_f), dtype)
+    B = orc.round_to(rng.standard_normal((out_f, r)) * 0.01, dtype)
+    x = orc.round_to(rng.standard_normal((T, in_f)), dtype)
+    dy = orc.round_to(rng.standard_normal((T, out_f)), dtype)
+    s = 2.0
+    tdt = to_dev(W, dtype).dtype
+    base = torch.nn.Linear(in_f, out_f, bias=False, device="cuda", dtype=tdt)
+    with torch.no_grad():
+        base.weight.copy_(to_dev(W, dtype))
+    mod = DoraLinear(base, r=r, scaling=s)
+    with torch.no_grad():
+        mod.lora_A.weight.copy_(to_dev(A, dtype))
+        mod.lora_B.weight.copy_(to_dev(B, dtype))
+        mod.reset_magnitude()
+    m = to_np(mod.lora_magnitude_vector.weight)
+    tx = to_dev(x, dtype).requires_grad_(True)
+    y = mod(tx)
+    y.backward(to_dev(dy, dtype))
+    ref = orc.dora_linear_forward_backward(x, W, None, A, B, m, s, dy, dtype)
+    assert_close(to_np(y), ref["y"], RTOL[dtype], "y")
+    assert_close(to_np(tx.grad), ref["dx"], RTOL[dtype], "dx")
+    assert_close(to_np(mod.lora_A.weight.grad), ref["dA"], RTOL[dtype], "dA")
+    assert_close(to_np(mod.lora_B.weight.grad), ref["dB"], RTOL[dtype], "dB")
+    assert_close(to_np(mod.lora_magnitude_vector.weight.grad), ref["dm"], RTOL[dtype], "dm")
+
+
+def test_no_base_result_path_matches():
+    """The dropout path (no precomputed base output) gives the same delta as the common path."""
+    st = LAYER["layer_bias_fp32"]
+    base, lora_A, lora_B, layer = _build(st, "fp32")
+    x = to_dev(st["x"], "fp32")
+    s = float(st["scale"])
+    with torch.no_grad():
+        d1 = layer(x, lora_A=lora_A, lora_B=lora_B, scaling=s, base_layer=base, base_result=base(x))
+        d2 = layer(x, lora_A=lora_A, lora_B=lora_B, scaling=s, base_layer=base, base_result=None)
+    assert_close(to_np(d2), to_np(d1), 1e-5, "delta")
+    assert layer._last_forward_chunk_size == base.out_features
+
+
+def test_inference_in_place_compose():
+    """No-grad forward composes in place into the LoRA output buffer."""
+    st = LAYER["layer_bf16"]
+    base, lora_A, lora_B, layer = _build(st, "bf16")
+    x = to_dev(st["x"], "bf16")
+    with torch.no_grad():
+        delta = layer(x, lora_A=lora_A, lora_B=lora_B, scaling=float(st["scale"]), base_layer=base,
+                      base_result=base(x))
+    assert_close(to_np(delta), st["delta"], 1e-2, "delta")

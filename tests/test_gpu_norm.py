@@ -1,0 +1,173 @@
+"""Factored row norm (tcgen05 path for bf16/fp16, CUDA-core path otherwise)
+through the C ABI, against the oracle, the reference's golden fixtures and a
+PyTorch fp32 evaluation on the GPU at the full layer sizes.
+
+Tolerance: norms within 1e-2 relative (elementwise) in bf16/fp16 and 1e-5 in
+fp32.  The fp32 intermediate terms are checked tighter where the path allows.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from _golden import RTOL, assert_close, load_group, to_dev, to_np
+from oracle import dora_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+NORM = load_group("norm")
+ASSEMBLY = load_group("assembly")
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    from dorafactors_b200 import _native
+
+    yield
+    assert _native.device_error(reset=True) == 0
+
+
+def _native_norm(W, A, B, s, dtype, adt=None, parts=True):
+    from dorafactors_b200 import _native
+
+    adt = adt or dtype
+    tW, tA, tB = to_dev(W, dtype), to_dev(A, adt), to_dev(B, adt)
+    out = torch.empty(W.shape[0], dtype=tW.dtype, device="cuda")
+    p = torch.empty(3 * W.shape[0], dtype=torch.float32, device="cuda") if parts else None
+    _native.weight_norm(tW, tA, tB, s, out, p)
+    return to_np(out), (to_np(p).reshape(3, -1) if parts else None)
+
+
+def _elem_rel(a, ref):
+    a = np.asarray(a, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(a - ref) / np.maximum(np.abs(ref), 1e-30)))
+
+
+@pytest.mark.parametrize("case", sorted(NORM))
+def test_norm_golden(case):
+    from dorafactors_b200.dora import DoraLinearLayer
+
+    st = NORM[case]
+    dt = st["dtype"]
+    layer = DoraLinearLayer(fan_in_fan_out=bool(st["fan_in_fan_out"]))
+    n = layer._get_weight_norm_linear(
+        base_weight=to_dev(st["W"], dt), lora_A_w=to_dev(st["A"], dt), lora_B_w=to_dev(st["B"], dt),
+        scaling=float(st["scale"]),
+    )
+    assert n.dtype == to_dev(st["W"], dt).dtype
+    assert _elem_rel(to_np(n), st["norm"]) <= RTOL[dt], case
+    lw = to_dev(st["B"] @ st["A"], "fp32")
+    nd = layer.get_weight_norm(to_dev(st["W"], dt), lw, float(st["scale"]))
+    assert _elem_rel(to_np(nd), st["norm_dense"]) <= RTOL[dt], case
+
+
+@pytest.mark.parametrize("case", sorted(ASSEMBLY))
+def test_assembly_bitwise_vs_oracle(case):
+    from dorafactors_b200.dora_fused import fused_norm_assembly
+
+    st = ASSEMBLY[case]
+    s = float(st["scale"])
+    (n,) = fused_norm_assembly(to_dev(st["w"], "fp32"), to_dev(st["c"], "fp32"), to_dev(st["b"], "fp32"), s)
+    np.testing.assert_array_equal(to_np(n), orc.assemble_norm(st["w"], st["c"], st["b"], s))
+
+
+# (out, in, r, dtype): tensor-core shapes (in % 8 == 0), ragged M tiles, r from
+# 1 to 520, and shapes that take the CUDA-core path (fp32, in % 8 != 0).
+CASES = [
+    (128, 64, 16, "bf16"),
+    (300, 256, 8, "bf16"),
+    (1000, 1024, 64, "bf16"),
+    (513, 2048, 384, "bf16"),
+    (256, 512, 520, "bf16"),
+    (384, 768, 100, "bf16"),
+    (200, 1000, 24, "fp16"),
+    (640, 4096, 256, "fp16"),
+    (96, 72, 1, "bf16"),
+    (130, 100, 12, "bf16"),
+    (257, 320, 40, "fp32"),
+    (64, 4096, 128, "fp32"),
+]
+
+
+@pytest.mark.parametrize("out_f,in_f,r,dtype", CASES)
+def test_norm_vs_oracle(out_f, in_f, r, dtype):
+    rng = np.random.default_rng(out_f * 7 + in_f + r)
+    W = orc.round_to(rng.standard_normal((out_f, in_f)) * 0.02, dtype)
+    A = orc.round_to(rng.uniform(-1, 1, (r, in_f)) / np.sqrt(in_f), dtype)
+    B = orc.round_to(rng.standard_normal((out_f, r)) * 0.01, dtype)
+    s = 1.5
+    n, parts = _native_norm(W, A, B, s, dtype)
+    ref, rp = orc.weight_norm_factored(W, A, B, s, dtype)
+    assert _elem_rel(n, ref) <= RTOL[dtype]
+    # The fp32 intermediate terms, normwise.
+    assert_close(parts[0], rp["w_norm_sq"], 1e-5, "||W||^2")
+    assert_close(parts[1], rp["cross"], 1e-4 if dtype != "fp32" else 1e-5, "cross")
+    assert_close(parts[2], rp["ba"], 1e-4 if dtype != "fp32" else 1e-5, "B G B^T")
+
+
+def test_norm_large_lora_term():
+    """A LoRA term as large as W0 exercises the cross and B G B^T terms at full weight."""
+    rng = np.random.default_rng(21)
+    out_f, in_f, r = 384, 1024, 64
+    W = orc.round_to(rng.standard_normal((out_f, in_f)) * 0.02, "bf16")
+    A = orc.round_to(rng.uniform(-1, 1, (r, in_f)) / np.sqrt(in_f), "bf16")
+    B = orc.round_to(rng.standard_normal((out_f, r)) * 0.5, "bf16")
+    for s in (0.5, 2.0, -1.0):
+        n, _ = _native_norm(W, A, B, s, "bf16")
+        dense = orc.weight_norm_dense(W, B.astype(np.float64) @ A.astype(np.float64), s, "fp32")
+        assert _elem_rel(n, dense) <= 1e-2
+
+
+def test_norm_scale_zero_and_rank_zero():
+    rng = np.random.default_rng(2)
+    W = orc.round_to(rng.standard_normal((200, 512)) * 0.02, "bf16")
+    A = orc.round_to(rng.standard_normal((16, 512)), "bf16")
+    B = orc.round_to(rng.standard_normal((200, 16)), "bf16")
+    n, parts = _native_norm(W, A, B, 0.0, "bf16")
+    ref, _ = orc.weight_norm_factored(W, A, B, 0.0, "bf16")
+    assert _elem_rel(n, ref) <= 1e-2
+    assert np.all(parts[1] == 0) and np.all(parts[2] == 0)
+
+
+def test_norm_mixed_adapter_dtype():
+    """bf16 W0 with fp32 adapters (PEFT's default adapter dtype) takes the fp32 CUDA-core path."""
+    rng = np.random.default_rng(4)
+    W = orc.round_to(rng.standard_normal((256, 512)) * 0.02, "bf16")
+    A = (rng.uniform(-1, 1, (32, 512)) / np.sqrt(512)).astype(np.float32)
+    B = (rng.standard_normal((256, 32)) * 0.01).astype(np.float32)
+    n, _ = _native_norm(W, A, B, 2.0, "bf16", adt="fp32")
+    ref, _ = orc.weight_norm_factored(W, A, B, 2.0, "bf16")
+    assert _elem_rel(n, ref) <= 1e-2
+
+
+def _torch_fp32_norm_parts(W, A, B):
+    Wf, Af, Bf = W.float(), A.float(), B.float()
+    w = (Wf * Wf).sum(1)
+    U = Wf @ Af.T
+    G = Af @ Af.T
+    c = (Bf * U).sum(1)
+    b = ((Bf @ G) * Bf).sum(1)
+    return w, c, b
+
+
+@pytest.mark.parametrize("out_f,in_f,r", [(28672, 8192, 384), (8192, 8192, 1024), (8192, 8192, 16)])
+def test_norm_full_size_vs_torch_fp32(out_f, in_f, r):
+    """Layer sizes of the benchmark: the tcgen05 result against PyTorch fp32 GEMMs on the same GPU."""
+    from dorafactors_b200 import _native
+
+    torch.manual_seed(0)
+    W = (torch.randn(out_f, in_f, device="cuda") * 0.02).bfloat16()
+    A = ((torch.rand(r, in_f, device="cuda") * 2 - 1) / in_f**0.5).bfloat16()
+    B = (torch.randn(out_f, r, device="cuda") * 0.01).bfloat16()
+    norm = torch.empty(out_f, dtype=torch.bfloat16, device="cuda")
+    parts = torch.empty(3 * out_f, dtype=torch.float32, device="cuda")
+    _native.weight_norm(W, A, B, 1.0, norm, parts)
+    w, c, b = _torch_fp32_norm_parts(W, A, B)
+    p = parts.view(3, -1)
+    for got, ref, tol in ((p[0], w, 1e-5), (p[1], c, 1e-4), (p[2], b, 1e-4)):
+        rel = ((got.double() - ref.double()).norm() / ref.double().norm()).item()
+        assert rel <= tol, rel
+    ref_norm = torch.sqrt((w + 2 * c + b).clamp_min(0)).bfloat16()
+    rel = ((norm.float() - ref_norm.float()).abs() / ref_norm.float()).max().item()
+    assert rel <= 1e-2
