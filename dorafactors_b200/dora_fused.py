@@ -67,9 +67,9 @@ def _prepare(lora: torch.Tensor, base: torch.Tensor, mag: torch.Tensor, what: st
     if lora.ndim == 0:
         raise ValueError(f"{what}: activations must have at least one dimension")
     cols = lora.shape[-1]
+    if mag.numel() != cols:
+        raise ValueError(f"mag_norm_scale has {mag.numel()} elements != num_cols {cols}")
     if not _mag_broadcasts_last_dim(mag, lora):
-        if mag.numel() == cols:
-            raise ValueError(f"mag_norm_scale shape {tuple(mag.shape)} does not broadcast along the last dim")
         raise NotImplementedError(
             f"{what}: mag_norm_scale {tuple(mag.shape)} does not broadcast along the last dim of "
             f"{tuple(lora.shape)}; only the linear layout (g over out_features) is implemented"
