@@ -39,6 +39,7 @@ SIGNATURES = {
     "dora_compose_fwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _int, _vp]),
     "dora_compose_bwd_workspace_size": (_sz, [_i64, _i64, _int]),
     "dora_compose_bwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
+    "dora_compose_bwd_noalloc": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "dora_norm_assembly": (_int, [_vp, _vp, _vp, _dbl, _vp, _i64, _vp]),
     "dora_weight_norm_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int]),
     "dora_weight_norm": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _int, _dbl, _vp, _vp, _vp, _sz, _vp]),

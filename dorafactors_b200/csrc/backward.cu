@@ -243,3 +243,71 @@ extern "C" int dora_compose_bwd(const void* d_out, const void* inner, const void
                                       cols, st);
   }
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of dora_compose_bwd.
+//
+// Some callers cannot hand this library a device workspace: a C or FFI host
+// that embeds the library without any device allocator of its own, or code
+// that must not call cudaMalloc on this path because cudaMalloc synchronizes
+// the device.  For them the column-sum scratch lives in a fixed array in this
+// library's device image instead.  The array exists once per GPU that loads
+// the library and stays allocated until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace dora {
+
+constexpr size_t kStaticScratchBytes = size_t(DORA_NOALLOC_SCRATCH_BYTES);
+static __device__ __align__(256) unsigned char g_bwd_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+static std::mutex g_scratch_mutex;
+static void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_bwd_scratch on the current device.  In host code the
+// symbol's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+static int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  if (dev < 0 || dev >= kMaxDevices) return DORA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_bwd_scratch);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return DORA_OK;
+}
+
+}  // namespace dora
+
+extern "C" int dora_compose_bwd_noalloc(const void* d_out, const void* inner, const void* g, int g_dtype,
+                                        double scale, void* d_lora, void* d_base, void* d_g, int64_t rows,
+                                        int64_t cols, int act_dtype, void* stream) {
+  if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
+  if (!d_g || rows == 0 || cols == 0) {
+    // No column sum (or nothing to sum over): no scratch is touched.
+    return dora_compose_bwd(d_out, inner, g, g_dtype, scale, d_lora, d_base, d_g, nullptr, 0, rows, cols,
+                            act_dtype, stream);
+  }
+  const size_t need = dora_compose_bwd_workspace_size(rows, cols, act_dtype);
+  if (need > kStaticScratchBytes) return DORA_ERR_WORKSPACE;
+  void* ws = nullptr;
+  int rc = static_scratch_address(&ws);
+  if (rc != DORA_OK) return rc;
+  // The scratch keeps whatever the last call left in it.  Only the completion
+  // counters at its start must begin at zero; clear them on this stream (the
+  // column partials are always written before they are read).
+  const size_t c_vec = bwd_plan(rows, cols, dtype_size(act_dtype), true).counter_bytes;
+  const size_t c_any = bwd_plan(rows, cols, dtype_size(act_dtype), false).counter_bytes;
+  const size_t counter_bytes = c_vec > c_any ? c_vec : c_any;
+  cudaError_t e = cudaMemsetAsync(ws, 0, counter_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_cuda_error(e);
+  return dora_compose_bwd(d_out, inner, g, g_dtype, scale, d_lora, d_base, d_g, ws, kStaticScratchBytes, rows,
+                          cols, act_dtype, stream);
+}

@@ -110,6 +110,38 @@ int dora_compose_bwd(const void* d_out, const void* inner, const void* g, int g_
                      int64_t rows, int64_t cols, int act_dtype, void* stream);
 
 /*
+ * Size of the fixed device scratch array behind dora_compose_bwd_noalloc:
+ * 4 MiB, held once on every GPU that loads the library.
+ */
+#define DORA_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/*
+ * dora_compose_bwd without a caller workspace.  This entry point has no
+ * counterpart in the reference.
+ *
+ * It is for callers that cannot allocate device memory for the column-sum
+ * scratch: a C or FFI host that embeds this library with no device allocator
+ * of its own, or code that must not call cudaMalloc here because cudaMalloc
+ * synchronizes the device.  Same arguments and results as dora_compose_bwd,
+ * minus the workspace; no cudaMalloc, cudaFree or other allocating call is
+ * made.  The scratch is a fixed DORA_NOALLOC_SCRATCH_BYTES array inside the
+ * library's device image; a shape whose dora_compose_bwd_workspace_size()
+ * exceeds it is rejected with DORA_ERR_WORKSPACE before anything is queued.
+ *
+ * The first call on each device looks up the array's device address (with
+ * that device current) and caches it; make that first call before any stream
+ * capture.  Every call shares the one array per device and it keeps the last
+ * call's contents: each call clears its completion counters on the given
+ * stream first.  Calls that overlap on the GPU (different streams, or
+ * different host threads without ordering) race on the array and give wrong
+ * d_g; order them on one stream or use dora_compose_bwd with separate
+ * workspaces instead.
+ */
+int dora_compose_bwd_noalloc(const void* d_out, const void* inner, const void* g, int g_dtype, double scale,
+                             void* d_lora, void* d_base, void* d_g, int64_t rows, int64_t cols, int act_dtype,
+                             void* stream);
+
+/*
  * Norm assembly: norm[i] = sqrt(max(w[i] + (2s)*c[i] + (s*s)*b[i], 0)) in
  * fp32, four separately rounded ops in that order, NaN kept by the clamp,
  * IEEE square root.
