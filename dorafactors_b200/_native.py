@@ -39,6 +39,8 @@ SIGNATURES = {
     "dora_compose_fwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _int, _vp]),
     "dora_compose_bwd_workspace_size": (_sz, [_i64, _i64, _int]),
     "dora_compose_bwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
+    "dora_linear_output_fwd": (_int, [_vp, _vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _int, _vp]),
+    "dora_linear_output_bwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
     "dora_compose_bwd_noalloc": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "dora_norm_assembly": (_int, [_vp, _vp, _vp, _dbl, _vp, _i64, _vp]),
     "dora_weight_norm_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int]),
@@ -193,6 +195,30 @@ def compose_bwd(d_out2d, inner2d, g1d, scale: float, d_lora2d, d_base2d, d_g1d) 
         ptr(d_g1d), ptr(ws), nbytes, rows, cols, act, stream_ptr(dev),
     )
     check(code, "dora_compose_bwd")
+
+
+def linear_output_fwd(lora2d, result2d, bias1d, g1d, scale: float, y2d, inner2d) -> None:
+    dev = lora2d.device
+    rows, cols = lora2d.shape
+    code = load_library().dora_linear_output_fwd(
+        ptr(lora2d), ptr(result2d), ptr(bias1d), ptr(g1d), dtype_code(g1d), float(scale), ptr(y2d), ptr(inner2d),
+        rows, cols, dtype_code(lora2d), stream_ptr(dev),
+    )
+    check(code, "dora_linear_output_fwd")
+
+
+def linear_output_bwd(d_y2d, inner2d, g1d, scale: float, d_lora2d, d_result2d, d_g1d) -> None:
+    dev = d_y2d.device
+    rows, cols = d_y2d.shape
+    act = dtype_code(d_y2d)
+    ws, nbytes = (None, 0)
+    if d_g1d is not None:
+        ws, nbytes = bwd_workspace(dev, rows, cols, act)
+    code = load_library().dora_linear_output_bwd(
+        ptr(d_y2d), ptr(inner2d), ptr(g1d), dtype_code(g1d), float(scale), ptr(d_lora2d), ptr(d_result2d),
+        ptr(d_g1d), ptr(ws), nbytes, rows, cols, act, stream_ptr(dev),
+    )
+    check(code, "dora_linear_output_bwd")
 
 
 def norm_assembly(w, c, b, scale: float, out) -> None:

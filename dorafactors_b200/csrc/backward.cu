@@ -17,7 +17,9 @@
 
 namespace dora {
 
-template <typename TA, typename TG, int VEC, bool kDL, bool kDB, bool kDG>
+// kRG selects the layer-output form: the second gradient is d_result = g * d_y
+// (the base branch of y = result + delta) instead of d_base = (g - 1) * d_out.
+template <typename TA, typename TG, int VEC, bool kDL, bool kDB, bool kDG, bool kRG>
 __global__ void __launch_bounds__(256)
 compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, const TG* __restrict__ g, float s,
                    TA* __restrict__ d_lora, TA* __restrict__ d_base, TG* __restrict__ d_g,
@@ -32,7 +34,7 @@ compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, c
   for (int k = 0; k < VEC; ++k) {
     const float gv = active ? to_f32(g[vc * VEC + k]) : 0.f;
     gs[k] = __fmul_rn(gv, s);
-    gm1[k] = __fsub_rn(gv, 1.0f);
+    gm1[k] = kRG ? gv : __fsub_rn(gv, 1.0f);
     acc[k] = 0.f;
   }
   const int64_t row0 = int64_t(blockIdx.y) * blockDim.y + threadIdx.y;
@@ -145,22 +147,22 @@ static BwdPlan bwd_plan(int64_t rows, int64_t cols, int esize, bool aligned) {
   return p;
 }
 
-template <typename TA, typename TG, int V, bool DL, bool DB, bool DG>
+template <typename TA, typename TG, int V, bool DL, bool DB, bool DG, bool RG>
 static void launch_bwd_v(const BwdPlan& p, const void* d_out, const void* inner, const void* g, float s,
                          void* d_lora, void* d_base, void* d_g, unsigned* cnt, float* part, int64_t rows,
                          cudaStream_t st) {
-  compose_bwd_kernel<TA, TG, V, DL, DB, DG><<<p.sh.grid, p.sh.block, 0, st>>>(
+  compose_bwd_kernel<TA, TG, V, DL, DB, DG, RG><<<p.sh.grid, p.sh.block, 0, st>>>(
       static_cast<const TA*>(d_out), static_cast<const TA*>(inner), static_cast<const TG*>(g), s,
       static_cast<TA*>(d_lora), static_cast<TA*>(d_base), static_cast<TG*>(d_g), cnt, part, rows, p.vcols);
 }
 
-template <typename TA, typename TG, int V>
+template <typename TA, typename TG, int V, bool RG>
 static void launch_bwd_sel(const BwdPlan& p, const void* d_out, const void* inner, const void* g, float s,
                            void* d_lora, void* d_base, void* d_g, unsigned* cnt, float* part, int64_t rows,
                            cudaStream_t st) {
   const int sel = (d_lora ? 4 : 0) | (d_base ? 2 : 0) | (d_g ? 1 : 0);
 #define DORA_BWD_CASE(n, a, b, c) \
-  case n: launch_bwd_v<TA, TG, V, a, b, c>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st); break;
+  case n: launch_bwd_v<TA, TG, V, a, b, c, RG>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st); break;
   switch (sel) {
     DORA_BWD_CASE(1, false, false, true)
     DORA_BWD_CASE(2, false, true, false)
@@ -174,7 +176,7 @@ static void launch_bwd_sel(const BwdPlan& p, const void* d_out, const void* inne
 #undef DORA_BWD_CASE
 }
 
-template <typename TA, typename TG>
+template <typename TA, typename TG, bool RG>
 static int launch_bwd(const void* d_out, const void* inner, const void* g, float s, void* d_lora, void* d_base,
                       void* d_g, void* ws, size_t ws_bytes, int64_t rows, int64_t cols, cudaStream_t st) {
   const bool aligned = aligned16(d_out) && (!inner || aligned16(inner)) && (!d_lora || aligned16(d_lora)) &&
@@ -189,8 +191,8 @@ static int launch_bwd(const void* d_out, const void* inner, const void* g, float
     part = reinterpret_cast<float*>(static_cast<char*>(ws) + p.counter_bytes);
   }
   constexpr int V = 16 / sizeof(TA);
-  if (p.vec) launch_bwd_sel<TA, TG, V>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st);
-  else launch_bwd_sel<TA, TG, 1>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st);
+  if (p.vec) launch_bwd_sel<TA, TG, V, RG>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st);
+  else launch_bwd_sel<TA, TG, 1, RG>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st);
   return check_launch();
 }
 
@@ -207,9 +209,12 @@ extern "C" size_t dora_compose_bwd_workspace_size(int64_t rows, int64_t cols, in
   return na > nb ? na : nb;
 }
 
-extern "C" int dora_compose_bwd(const void* d_out, const void* inner, const void* g, int g_dtype, double scale,
-                                void* d_lora, void* d_base, void* d_g, void* workspace, size_t workspace_bytes,
-                                int64_t rows, int64_t cols, int act_dtype, void* stream) {
+namespace dora {
+
+template <bool RG>
+static int bwd_entry(const void* d_out, const void* inner, const void* g, int g_dtype, double scale, void* d_lora,
+                     void* d_base, void* d_g, void* workspace, size_t workspace_bytes, int64_t rows, int64_t cols,
+                     int act_dtype, void* stream) {
   if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
   if (g_dtype != act_dtype && g_dtype != DORA_DTYPE_F32) return DORA_ERR_INVALID_ARGUMENT;
   if (!d_lora && !d_base && !d_g) return DORA_OK;
@@ -228,20 +233,37 @@ extern "C" int dora_compose_bwd(const void* d_out, const void* inner, const void
   switch (act_dtype) {
     case DORA_DTYPE_BF16:
       return g_dtype == DORA_DTYPE_F32
-                 ? launch_bwd<__nv_bfloat16, float>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
-                                                    workspace_bytes, rows, cols, st)
-                 : launch_bwd<__nv_bfloat16, __nv_bfloat16>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
-                                                            workspace_bytes, rows, cols, st);
+                 ? launch_bwd<__nv_bfloat16, float, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
+                                                        workspace_bytes, rows, cols, st)
+                 : launch_bwd<__nv_bfloat16, __nv_bfloat16, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
+                                                                workspace_bytes, rows, cols, st);
     case DORA_DTYPE_F16:
       return g_dtype == DORA_DTYPE_F32
-                 ? launch_bwd<__half, float>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes,
-                                             rows, cols, st)
-                 : launch_bwd<__half, __half>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes,
-                                              rows, cols, st);
+                 ? launch_bwd<__half, float, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes,
+                                                 rows, cols, st)
+                 : launch_bwd<__half, __half, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
+                                                  workspace_bytes, rows, cols, st);
     default:
-      return launch_bwd<float, float>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes, rows,
-                                      cols, st);
+      return launch_bwd<float, float, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes, rows,
+                                          cols, st);
   }
+}
+
+}  // namespace dora
+
+extern "C" int dora_compose_bwd(const void* d_out, const void* inner, const void* g, int g_dtype, double scale,
+                                void* d_lora, void* d_base, void* d_g, void* workspace, size_t workspace_bytes,
+                                int64_t rows, int64_t cols, int act_dtype, void* stream) {
+  return bwd_entry<false>(d_out, inner, g, g_dtype, scale, d_lora, d_base, d_g, workspace, workspace_bytes, rows,
+                          cols, act_dtype, stream);
+}
+
+extern "C" int dora_linear_output_bwd(const void* d_y, const void* inner, const void* g, int g_dtype, double scale,
+                                      void* d_lora, void* d_result, void* d_g, void* workspace,
+                                      size_t workspace_bytes, int64_t rows, int64_t cols, int act_dtype,
+                                      void* stream) {
+  return bwd_entry<true>(d_y, inner, g, g_dtype, scale, d_lora, d_result, d_g, workspace, workspace_bytes, rows,
+                         cols, act_dtype, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -52,7 +52,7 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     const TcGemmShape g = tc_gemm_shape(r, r, in);
     const int64_t tiles = int64_t(g.m_tiles) * g.n_tiles;
     int s = int(sms / (tiles > 0 ? tiles : 1));
-    const int cap = g.kblocks / 4 > 0 ? g.kblocks / 4 : 1;
+    const int cap = g.kblocks / 8 > 0 ? g.kblocks / 8 : 1;
     p.gram_splits = s < 1 ? 1 : (s > cap ? cap : s);
   } else {
     const int64_t tiles = ((r + 63) / 64) * ((r + 63) / 64);

@@ -146,7 +146,8 @@ __host__ __device__ inline SmemLayout smem_layout(int nt, int stages) {
 template <typename T, int MODE, bool kSumSq>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY1,
-                 const __grid_constant__ CUtensorMap tmY2, int two_y, const T* __restrict__ Z, int64_t ldz,
+                 const __grid_constant__ CUtensorMap tmY2, const __grid_constant__ CUtensorMap tmZ, int z_tma,
+                 int two_y, const T* __restrict__ Z, int64_t ldz,
                  int64_t M, int64_t N, int nt, int ybox, int n_tiles, int m_tiles, int kblocks, int k_splits,
                  int stages, uint32_t tmem_cols, float* __restrict__ rowdot_part, float* __restrict__ sumsq_part,
                  float* __restrict__ C) {
@@ -157,7 +158,8 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
   uint64_t* drain = done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* zfull = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(zfull + 1);
   volatile int* aborted = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -181,6 +183,7 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
     }
     mbar_init(done, 1);
     mbar_init(drain, 1);
+    mbar_init(zfull, 1);
     *aborted = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -221,6 +224,20 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
         // Let every load this thread issued land before the CTA's shared memory is released.
         for (int it = issued - stages > 0 ? issued - stages : 0; it < issued; ++it)
           mbar_wait(&full[it % stages], (it / stages) & 1);
+      } else if (z_tma) {
+        // Stage this tile's rows of Z (= B) for the epilogue in the ring, once the
+        // last MMAs (and row-sum readers) have released every slot.
+        bool free_ring = true;
+        for (int it = iters - stages > 0 ? iters - stages : 0; it < iters && free_ring; ++it)
+          free_ring = mbar_wait(&empty[it % stages], (it / stages) & 1);
+        if (!free_ring) {
+          *aborted = 1;
+        } else {
+          const int nzb = (nt + BK - 1) / BK;
+          mbar_expect_tx(zfull, uint32_t(nzb) * kXTileBytes);
+          for (int j = 0; j < nzb; ++j) tma_load_2d(base + size_t(j) * kXTileBytes, &tmZ, zfull, int(n0) + j * BK, int(m0));
+          mbar_wait(zfull, 0);  // keep this thread until the copies have landed
+        }
       }
     }
   } else if (warp == 1) {
@@ -278,7 +295,7 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
         if (lane == 0) mbar_arrive(&empty[s]);
       }
     }
-    const bool ok = !*aborted && mbar_wait(done, 0);
+    const bool ok = !*aborted && mbar_wait(done, 0) && (!z_tma || mbar_wait(zfull, 0));
     if (ok) {
       tc_fence_after();
       const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16);
@@ -292,7 +309,20 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
           const int cnt = (N - nbase) < 32 ? int(N - nbase) : 32;
           if constexpr (MODE == kGemmRowdot) {
             const T* zr = Z + m * ldz + nbase;
-            if (cnt == 32 && ((reinterpret_cast<uintptr_t>(zr) & 15u) == 0)) {
+            if (z_tma) {
+              // Row `row` of the staged Z tile: 64-column boxes of 128-byte rows with the
+              // 16-byte chunks of row r stored at chunk ^ (r % 8).
+              const uint8_t* zrow = base + size_t(c0 / BK) * kXTileBytes + row * 128;
+              const int q0 = (c0 % BK) / 8;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 zv = *reinterpret_cast<const uint4*>(zrow + (((q0 + j) ^ (row & 7)) * 16));
+                const T* zh = reinterpret_cast<const T*>(&zv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  if (j * 8 + e < cnt) acc = fmaf(v[j * 8 + e], to_f32(zh[e]), acc);
+              }
+            } else if (cnt == 32 && ((reinterpret_cast<uintptr_t>(zr) & 15u) == 0)) {
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const uint4 zv = __ldg(reinterpret_cast<const uint4*>(zr) + j);
@@ -404,7 +434,8 @@ bool tc_gemm_supported(int dtype, int64_t M, int64_t N, int64_t K, const void* X
 
 template <typename T, int MODE, bool SSQ>
 static int launch_tc(const TcGemmArgs& a, const TcGemmShape& sh, const CUtensorMap& mx, const CUtensorMap& my1,
-                     const CUtensorMap& my2, int ybox, int stages, cudaStream_t st) {
+                     const CUtensorMap& my2, const CUtensorMap& mz, int z_tma, int ybox, int stages,
+                     cudaStream_t st) {
   const tc::SmemLayout L = tc::smem_layout(sh.nt, stages);
   auto kfn = tc::tc_rowdot_kernel<T, MODE, SSQ>;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
@@ -412,7 +443,7 @@ static int launch_tc(const TcGemmArgs& a, const TcGemmShape& sh, const CUtensorM
   uint32_t cols = 32;
   while (cols < uint32_t(sh.nt)) cols <<= 1;
   const unsigned grid = unsigned(sh.m_tiles) * unsigned(sh.n_tiles) * unsigned(a.k_splits);
-  kfn<<<grid, tc::kThreads, L.total, st>>>(mx, my1, my2, a.Y2 ? 1 : 0, static_cast<const T*>(a.Z), a.ldz, a.M, a.N,
+  kfn<<<grid, tc::kThreads, L.total, st>>>(mx, my1, my2, mz, z_tma, a.Y2 ? 1 : 0, static_cast<const T*>(a.Z), a.ldz, a.M, a.N,
                                             sh.nt, ybox, sh.n_tiles, sh.m_tiles, sh.kblocks, a.k_splits, stages, cols,
                                             a.rowdot_part, a.sumsq_part, a.C);
   return check_launch();
@@ -420,10 +451,11 @@ static int launch_tc(const TcGemmArgs& a, const TcGemmShape& sh, const CUtensorM
 
 template <typename T>
 static int dispatch_tc(const TcGemmArgs& a, const TcGemmShape& sh, const CUtensorMap& mx, const CUtensorMap& my1,
-                       const CUtensorMap& my2, int ybox, int stages, cudaStream_t st) {
-  if (a.mode == kGemmStore) return launch_tc<T, kGemmStore, false>(a, sh, mx, my1, my2, ybox, stages, st);
-  if (a.sumsq) return launch_tc<T, kGemmRowdot, true>(a, sh, mx, my1, my2, ybox, stages, st);
-  return launch_tc<T, kGemmRowdot, false>(a, sh, mx, my1, my2, ybox, stages, st);
+                       const CUtensorMap& my2, const CUtensorMap& mz, int z_tma, int ybox, int stages,
+                       cudaStream_t st) {
+  if (a.mode == kGemmStore) return launch_tc<T, kGemmStore, false>(a, sh, mx, my1, my2, mz, 0, ybox, stages, st);
+  if (a.sumsq) return launch_tc<T, kGemmRowdot, true>(a, sh, mx, my1, my2, mz, z_tma, ybox, stages, st);
+  return launch_tc<T, kGemmRowdot, false>(a, sh, mx, my1, my2, mz, z_tma, ybox, stages, st);
 }
 
 int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st) {
@@ -436,8 +468,18 @@ int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st) {
       !tc::make_map(&my2, a.Y2 ? a.Y2 : a.Y1, a.dtype, a.N, a.K, ybox))
     return DORA_ERR_CUDA;
   const int stages = tc::stages_for(sh.nt);
-  if (a.dtype == DORA_DTYPE_BF16) return dispatch_tc<__nv_bfloat16>(a, sh, mx, my1, my2, ybox, stages, st);
-  return dispatch_tc<__half>(a, sh, mx, my1, my2, ybox, stages, st);
+  // The epilogue's Z rows come through TMA into the freed stage ring when Z's rows
+  // are 16-byte aligned (a 2-D map needs a 16-byte row stride) and the tile fits.
+  CUtensorMap mz = mx;
+  int z_tma = 0;
+  const uint32_t z_bytes = uint32_t((sh.nt + tc::BK - 1) / tc::BK) * tc::kXTileBytes;
+  if (a.mode == kGemmRowdot && a.Z && a.ldz == a.N && (a.ldz * 2) % 16 == 0 && aligned16(a.Z) &&
+      z_bytes <= tc::smem_layout(sh.nt, stages).bar_offset) {
+    if (!tc::make_map(&mz, a.Z, a.dtype, a.M, a.ldz, tc::BM)) return DORA_ERR_CUDA;
+    z_tma = 1;
+  }
+  if (a.dtype == DORA_DTYPE_BF16) return dispatch_tc<__nv_bfloat16>(a, sh, mx, my1, my2, mz, z_tma, ybox, stages, st);
+  return dispatch_tc<__half>(a, sh, mx, my1, my2, mz, z_tma, ybox, stages, st);
 }
 
 }  // namespace dora

@@ -281,5 +281,37 @@ class DoraLinearLayer(nn.Module):
             lora_out=lora_result, base_result=base_full, mag_norm_scale=mag_norm_scale, scale=scale
         )
 
+    def forward_output(self, x, *, lora_A, lora_B, scaling, base_layer, result):
+        """The layer output ``result + delta`` in one fused pass.
+
+        Equivalent to ``result + self.forward(x, ..., base_result=result)``, the
+        composition ``DoraLinearVariant.forward`` performs (variants.py:214-284), with
+        the add folded into the compose kernel and its backward.  ``result`` is the
+        base layer's output on ``x`` (bias included).
+        """
+        from .dora_fused import fused_dora_linear_output
+
+        magnitude = self.weight
+        with torch.no_grad(), _disable_autocast(base_layer.weight.device.type):
+            weight_norm = self._get_weight_norm_linear(
+                base_weight=base_layer.weight,
+                lora_A_w=lora_A.weight,
+                lora_B_w=lora_B.weight,
+                scaling=scaling,
+            )
+        if weight_norm.device != magnitude.device:
+            weight_norm = weight_norm.to(device=magnitude.device)
+        eps = 1e-12 if weight_norm.dtype in (torch.float32, torch.float64) else 1e-6
+        mag_norm_scale = (magnitude / weight_norm.clamp_min(eps)).view(1, -1)
+        lora_result = lora_B(lora_A(x))
+        g = mag_norm_scale
+        if g.dtype not in (lora_result.dtype, torch.float32):
+            g = g.float()
+        bias = base_layer.bias
+        self._last_forward_chunk_size = None
+        if result.dtype != lora_result.dtype:
+            result = result.to(lora_result.dtype)
+        return fused_dora_linear_output(lora_result, result, g, scaling, bias)
+
     def __repr__(self) -> str:
         return "lora.dora." + super().__repr__()

@@ -231,6 +231,99 @@ class FusedDoRAComposeFunction(torch.autograd.Function):
         return d_lora, d_base, d_mag, None
 
 
+class FusedDoRALinearOutputFunction(torch.autograd.Function):
+    """The adapted linear's output ``y = result + delta`` in one pass.
+
+    Forward: ``base = result - bias``, ``y = result + ((g - 1) * base + g * (s * lora))``
+    (what ``DoraLinearLayer.forward`` followed by ``DoraLinearVariant.forward``'s
+    ``result + delta`` computes, variants.py:244-283), plus ``inner = s * lora + base``
+    when ``g`` needs a gradient.  Backward: one pass giving ``d_lora = (g * s) * d_y``,
+    ``d_result = g * d_y`` (the direct path and the base path of ``result`` summed) and
+    ``d_g = sum_rows inner * d_y``.  The separate ``result + delta`` pass and
+    autograd's ``d_y + d_base`` accumulation disappear.
+    """
+
+    @staticmethod
+    def forward(ctx, lora, result, mag_norm_scale, scale, bias):
+        l, r, g, rows, cols = _prepare(lora, result, mag_norm_scale, "fused_dora_linear_output")
+        bvec = None
+        if bias is not None:
+            bvec = bias.detach().reshape(-1).to(device=l.device, dtype=l.dtype).contiguous()
+            if bvec.numel() != cols:
+                raise ValueError(f"bias has {bvec.numel()} elements != num_cols {cols}")
+        needs_mag = mag_norm_scale.requires_grad
+        with torch.no_grad():
+            y = torch.empty_like(l)
+            inner = torch.empty_like(l) if needs_mag else None
+            if rows and cols:
+                _native.linear_output_fwd(l.view(rows, cols), r.view(rows, cols), bvec, g, scale,
+                                          y.view(rows, cols), inner.view(rows, cols) if inner is not None else None)
+        ctx.needs_mag = needs_mag
+        ctx.scale = scale
+        ctx.has_bias = bias is not None
+        if needs_mag:
+            ctx.save_for_backward(inner, mag_norm_scale)
+        else:
+            ctx.save_for_backward(mag_norm_scale)
+        return y.view(lora.shape)
+
+    @staticmethod
+    def backward(ctx, d_y):
+        if ctx.needs_mag:
+            inner, mag = ctx.saved_tensors
+        else:
+            (mag,) = ctx.saved_tensors
+            inner = None
+        need_lora, need_result, need_mag = ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.needs_input_grad[2]
+        _native.require_cuda(d_y, inner, mag, what="FusedDoRALinearOutputFunction.backward")
+        cols = d_y.shape[-1]
+        rows = d_y.numel() // cols if cols else 0
+        act = d_y.dtype
+        g = mag.reshape(-1)
+        if g.dtype not in (act, torch.float32):
+            g = g.float()
+        g = g.contiguous()
+        d = d_y.contiguous()
+        d_lora = torch.empty_like(d) if need_lora else None
+        d_result = torch.empty_like(d) if need_result else None
+        d_g = None
+        inn = None
+        if need_mag:
+            inn = (inner if inner.dtype == act else inner.to(act)).contiguous()
+            d_g = torch.empty(cols, dtype=g.dtype, device=d.device)
+        if (need_lora or need_result or need_mag) and rows and cols:
+            _native.linear_output_bwd(
+                d.view(rows, cols), inn.view(rows, cols) if inn is not None else None, g, ctx.scale,
+                d_lora.view(rows, cols) if d_lora is not None else None,
+                d_result.view(rows, cols) if d_result is not None else None, d_g,
+            )
+        elif need_mag:
+            d_g.zero_()
+        d_bias = None
+        if ctx.has_bias and ctx.needs_input_grad[4]:
+            # y depends on the bias directly through base = result - bias.
+            d_bias = -((g.float() - 1) * d.float().reshape(rows, cols)).sum(0)
+        if d_lora is not None:
+            d_lora = d_lora.view(d_y.shape)
+        if d_result is not None:
+            d_result = d_result.view(d_y.shape)
+        if d_g is not None:
+            d_g = d_g.view(mag.shape)
+            if d_g.dtype != mag.dtype:
+                d_g = d_g.to(mag.dtype)
+        return d_lora, d_result, d_g, None, d_bias
+
+
+def fused_dora_linear_output(lora, result, mag_norm_scale, scale, bias=None):
+    """``result + DoRA delta`` in one native pass, with the fused backward.
+
+    ``result`` is the base layer's output including ``bias``; the delta uses
+    ``base = result - bias`` exactly as ``DoraLinearLayer.forward`` does
+    (dora.py:1443-1459).
+    """
+    return FusedDoRALinearOutputFunction.apply(lora, result, mag_norm_scale, scale, bias)
+
+
 def _broadcast_reduce_dims(out_shape: torch.Size, mag_shape: torch.Size) -> list:
     """Dims of *out_shape* broadcast from *mag_shape* (dora_fused.py:1209-1226)."""
     ndim_out, ndim_mag = len(out_shape), len(mag_shape)

@@ -50,18 +50,20 @@ class DoraLinear(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         result = self.base_layer(x)
         if isinstance(self.lora_dropout, nn.Identity) or not self.training:
-            base_result = result
-            xd = x
-        else:
-            xd = self.lora_dropout(x)
-            base_result = None
+            # The common path: the DoRA delta and the add to the base output are one
+            # native pass (forward) and one native pass (backward).
+            return self.lora_magnitude_vector.forward_output(
+                x, lora_A=self.lora_A, lora_B=self.lora_B, scaling=self.scaling, base_layer=self.base_layer,
+                result=result,
+            )
+        # Dropout active: the delta is formed from the dropped-out input, with the base
+        # output recomputed from it (dora.py:1155-1263), and added to the undropped
+        # result (variants.py:244-283).
+        xd = self.lora_dropout(x)
         delta = self.lora_magnitude_vector(
             xd, lora_A=self.lora_A, lora_B=self.lora_B, scaling=self.scaling, base_layer=self.base_layer,
-            base_result=base_result,
+            base_result=None,
         )
         if delta.dtype != result.dtype:
             delta = delta.to(result.dtype)
-        delta_depends_on_result = base_result is result and self.base_layer.bias is None
-        if delta_depends_on_result and torch.is_grad_enabled():
-            return result + delta
-        return result.add_(delta)
+        return result + delta

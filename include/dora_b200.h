@@ -110,6 +110,38 @@ int dora_compose_bwd(const void* d_out, const void* inner, const void* g, int g_
                      int64_t rows, int64_t cols, int act_dtype, void* stream);
 
 /*
+ * Compose forward with the base output added in the same pass (the layer
+ * output the PEFT variant forms as result + delta):
+ *   base[i,j]  = result[i,j] - bias[j]                  (bias may be NULL)
+ *   y[i,j]     = result[i,j] + ((g[j] - 1) * base[i,j] + g[j] * (scale * lora[i,j]))
+ *   inner[i,j] = scale * lora[i,j] + base[i,j]           (only if inner != NULL)
+ * fp32 arithmetic in that op order, one rounding per output (fp32 results equal
+ * the reference's result + delta bit for bit).  bias has act_dtype.  y may not
+ * alias result; y may alias lora only when inner is NULL.
+ *
+ * Replaces the compose of DoraLinearLayer.forward (dora.py:1443-1468) plus the
+ * result + delta / result.add_(delta) glue of DoraLinearVariant.forward
+ * (variants.py:244-283), one activation pass instead of three.
+ */
+int dora_linear_output_fwd(const void* lora, const void* result, const void* bias, const void* g, int g_dtype,
+                           double scale, void* y, void* inner, int64_t rows, int64_t cols, int act_dtype,
+                           void* stream);
+
+/*
+ * Backward of dora_linear_output_fwd, one pass over d_y (and inner):
+ *   d_lora[i,j]   = (g[j] * scale) * d_y[i,j]
+ *   d_result[i,j] = g[j] * d_y[i,j]      (both paths from y to result: 1 + (g - 1))
+ *   d_g[j]        = sum_i inner[i,j] * d_y[i,j]
+ * Same workspace rules as dora_compose_bwd (dora_compose_bwd_workspace_size).
+ *
+ * Replaces FusedDoRAComposeFunction.backward (dora_fused.py:1137-1206) plus
+ * autograd's accumulation of d_y and d_base into the base output's gradient.
+ */
+int dora_linear_output_bwd(const void* d_y, const void* inner, const void* g, int g_dtype, double scale,
+                           void* d_lora, void* d_result, void* d_g, void* workspace, size_t workspace_bytes,
+                           int64_t rows, int64_t cols, int act_dtype, void* stream);
+
+/*
  * Size of the fixed device scratch array behind dora_compose_bwd_noalloc:
  * 4 MiB, held once on every GPU that loads the library.
  */

@@ -237,3 +237,53 @@ def test_errors_are_loud():
         df.fused_dora_compose(x.cpu(), x.cpu(), torch.ones(1, 16, dtype=torch.bfloat16), 1.0)
     e = torch.empty(0, 16, device="cuda", dtype=torch.bfloat16)
     assert df.fused_dora_compose(e, e.clone(), torch.ones(16, device="cuda", dtype=torch.bfloat16), 1.0).numel() == 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
+@pytest.mark.parametrize("with_bias", [False, True])
+@pytest.mark.parametrize("rows,cols", [(5, 37), (300, 1000), (1024, 4096)])
+def test_linear_output_fused_glue(dtype, with_bias, rows, cols):
+    """y = result + delta in one pass, and its backward, against the oracle's eager
+    restatement of DoraLinearLayer.forward + DoraLinearVariant.forward."""
+    from dorafactors_b200 import dora_fused as df
+
+    rng = np.random.default_rng(rows * 3 + cols + with_bias)
+    lora, res = _rand(rng, (rows, cols), dtype), _rand(rng, (rows, cols), dtype)
+    g = _rand(rng, (1, cols), dtype, 0.5, 1.5)
+    bias = _rand(rng, (cols,), dtype) if with_bias else None
+    dy = _rand(rng, (rows, cols), dtype)
+    s = 1.5
+    tl = to_dev(lora, dtype).requires_grad_(True)
+    tr = to_dev(res, dtype).requires_grad_(True)
+    tg = to_dev(g, dtype).requires_grad_(True)
+    tb = to_dev(bias, dtype) if with_bias else None
+    y = df.fused_dora_linear_output(tl, tr, tg, s, tb)
+    y.backward(to_dev(dy, dtype))
+    # Oracle: base = result - bias, delta = eager compose, y = result + delta.
+    base = orc._op(np.subtract, dtype, res, bias[None, :]) if with_bias else res
+    delta = orc.compose_eager(lora, base, g, s, dtype, dtype)
+    ry = orc._op(np.add, dtype, res, delta)
+    if dtype == "fp32":
+        np.testing.assert_array_equal(to_np(y), ry)
+    else:
+        assert_close(to_np(y), ry, RTOL[dtype], "y")
+    # Gradients: d_lora = g s dy, d_result = dy + (g - 1) dy = g dy, d_g = sum inner * dy.
+    g64, d64 = g.astype(np.float64), dy.astype(np.float64)
+    inner64 = s * lora.astype(np.float64) + base.astype(np.float64)
+    assert_close(to_np(tl.grad), g64 * s * d64, RTOL[dtype], "d_lora")
+    assert_close(to_np(tr.grad), g64 * d64, RTOL[dtype], "d_result")
+    assert_close(to_np(tg.grad), (inner64 * d64).sum(0, keepdims=True), RTOL[dtype], "d_g")
+
+
+def test_linear_output_matches_two_pass_path():
+    """The fused layer output equals delta (native compose) + result in bf16 within rounding."""
+    from dorafactors_b200 import dora_fused as df
+
+    rng = np.random.default_rng(12)
+    lora, res = _rand(rng, (256, 2048), "bf16"), _rand(rng, (256, 2048), "bf16")
+    g = _rand(rng, (1, 2048), "bf16", 0.5, 1.5)
+    tl, tr, tg = to_dev(lora, "bf16"), to_dev(res, "bf16"), to_dev(g, "bf16")
+    with torch.no_grad():
+        y1 = df.fused_dora_linear_output(tl, tr, tg, 2.0)
+        y2 = tr + df.fused_dora_compose(tl.clone(), tr, tg, 2.0, inplace=False)
+    assert_close(to_np(y1), to_np(y2), 1e-2, "fused vs two-pass")

@@ -125,3 +125,56 @@ def test_inference_in_place_compose():
         delta = layer(x, lora_A=lora_A, lora_B=lora_B, scaling=float(st["scale"]), base_layer=base,
                       base_result=base(x))
     assert_close(to_np(delta), st["delta"], 1e-2, "delta")
+
+
+def test_dora_linear_with_bias_vs_oracle():
+    """Fused layer-output path with a base bias (base = result - bias inside the kernel)."""
+    from dorafactors_b200.layer import DoraLinear
+
+    dtype, T, in_f, out_f, r, s = "bf16", 128, 256, 384, 16, 0.5
+    rng = np.random.default_rng(99)
+    W = orc.round_to(rng.standard_normal((out_f, in_f)) * 0.02, dtype)
+    bias = orc.round_to(rng.standard_normal(out_f) * 0.1, dtype)
+    A = orc.round_to(rng.uniform(-1, 1, (r, in_f)) / np.sqrt(in_f), dtype)
+    B = orc.round_to(rng.standard_normal((out_f, r)) * 0.01, dtype)
+    x = orc.round_to(rng.standard_normal((T, in_f)), dtype)
+    dy = orc.round_to(rng.standard_normal((T, out_f)), dtype)
+    base = torch.nn.Linear(in_f, out_f, bias=True, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        base.weight.copy_(to_dev(W, dtype))
+        base.bias.copy_(to_dev(bias, dtype))
+    mod = DoraLinear(base, r=r, scaling=s)
+    with torch.no_grad():
+        mod.lora_A.weight.copy_(to_dev(A, dtype))
+        mod.lora_B.weight.copy_(to_dev(B, dtype))
+        mod.reset_magnitude()
+    m = to_np(mod.lora_magnitude_vector.weight)
+    tx = to_dev(x, dtype).requires_grad_(True)
+    y = mod(tx)
+    y.backward(to_dev(dy, dtype))
+    ref = orc.dora_linear_forward_backward(x, W, bias, A, B, m, s, dy, dtype)
+    for k, v in (("y", y), ("dx", tx.grad), ("dA", mod.lora_A.weight.grad), ("dB", mod.lora_B.weight.grad),
+                 ("dm", mod.lora_magnitude_vector.weight.grad)):
+        assert_close(to_np(v), ref[k], RTOL[dtype], k)
+
+
+def test_dora_linear_dropout_and_eval_paths():
+    """Training with dropout takes the two-pass path (delta from the dropped-out input);
+    eval mode takes the fused path and agrees with the two-pass composition."""
+    from dorafactors_b200.layer import DoraLinear
+
+    torch.manual_seed(3)
+    base = torch.nn.Linear(256, 320, bias=False, device="cuda", dtype=torch.bfloat16)
+    mod = DoraLinear(base, r=8, scaling=2.0, dropout=0.1, init_lora_B_zero=False)
+    x = torch.randn(64, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    mod.train()
+    y = mod(x)
+    y.float().square().sum().backward()
+    assert torch.isfinite(x.grad.float()).all() and mod.lora_magnitude_vector.weight.grad is not None
+    mod.eval()
+    with torch.no_grad():
+        y_eval = mod(x)
+        delta = mod.lora_magnitude_vector(x, lora_A=mod.lora_A, lora_B=mod.lora_B, scaling=2.0, base_layer=base,
+                                          base_result=base(x))
+        y_two = base(x) + delta
+    assert_close(to_np(y_eval), to_np(y_two), 1e-2, "eval fused vs two-pass")
