@@ -168,6 +168,7 @@ def bwd_workspace(device: torch.device, rows: int, cols: int, act_code: int) -> 
 def clear_workspace_cache() -> None:
     with _ws_lock:
         _ws_cache.clear()
+        _norm_ws_cache.clear()
 
 
 # ---------------------------------------------------------------------------
@@ -227,13 +228,28 @@ def norm_assembly(w, c, b, scale: float, out) -> None:
     check(code, "dora_norm_assembly")
 
 
+_norm_ws_cache: dict = {}
+
+
+def norm_workspace(device: torch.device, need: int) -> torch.Tensor:
+    """Scratch for dora_weight_norm, kept per (device, stream) and grown on demand.
+    Its contents never need clearing, so reuse on one stream is safe."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    with _ws_lock:
+        buf = _norm_ws_cache.get(key)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+            _norm_ws_cache[key] = buf
+    return buf
+
+
 def weight_norm(W, A, B, scale: float, norm_out, parts=None) -> None:
     lib = load_library()
     out_f, in_f = W.shape
     rank = A.shape[0]
     wd, ad, bd = dtype_code(W), dtype_code(A), dtype_code(B)
     need = lib.dora_weight_norm_workspace_size(out_f, in_f, rank, wd, ad, bd)
-    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=W.device)
+    ws = norm_workspace(W.device, need)
     code = lib.dora_weight_norm(
         ptr(W), ptr(A), ptr(B), out_f, in_f, rank, wd, ad, bd, float(scale), ptr(norm_out), ptr(parts),
         ptr(ws), need, stream_ptr(W.device),

@@ -18,6 +18,7 @@
 // Every mbarrier wait is bounded (about one second); on expiry the kernel
 // records DORA_ERR_DEVICE_TIMEOUT in the device error word, drains what it
 // issued and returns instead of hanging.  No cluster, no multicast.
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -31,6 +32,7 @@ constexpr int BK = 64;  // 64 half-precision elements = one 128-byte swizzle row
 constexpr int kThreads = 192;
 constexpr uint32_t kXTileBytes = BM * BK * 2;
 constexpr long long kWaitCycles = 1ll << 31;
+constexpr uint32_t kMaxDynamicSmem = 227u * 1024u;  // per-block opt-in limit on sm_100
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -438,8 +440,17 @@ static int launch_tc(const TcGemmArgs& a, const TcGemmShape& sh, const CUtensorM
                      cudaStream_t st) {
   const tc::SmemLayout L = tc::smem_layout(sh.nt, stages);
   auto kfn = tc::tc_rowdot_kernel<T, MODE, SSQ>;
-  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
+  // Opt in to the largest dynamic shared memory once per device for this kernel.
+  static std::atomic<unsigned long long> opted{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_cuda_error(e);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(opted.load(std::memory_order_relaxed) & bit)) {
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tc::kMaxDynamicSmem));
+    if (e != cudaSuccess) return set_cuda_error(e);
+    opted.fetch_or(bit, std::memory_order_relaxed);
+  }
   uint32_t cols = 32;
   while (cols < uint32_t(sh.nt)) cols <<= 1;
   const unsigned grid = unsigned(sh.m_tiles) * unsigned(sh.n_tiles) * unsigned(a.k_splits);

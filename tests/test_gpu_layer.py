@@ -178,3 +178,45 @@ def test_dora_linear_dropout_and_eval_paths():
                                           base_result=base(x))
         y_two = base(x) + delta
     assert_close(to_np(y_eval), to_np(y_two), 1e-2, "eval fused vs two-pass")
+
+
+def test_row_sharded_single_rank_matches_dora_linear():
+    """RowShardedDoraLinear on a one-rank NCCL group runs the native norm and fused
+    compose on its shard; with one rank the shard is the whole layer, so it must
+    match DoraLinear (the collectives are identities)."""
+    import datetime
+    import os
+    import socket
+
+    import torch.distributed as dist
+
+    from dorafactors_b200.layer import DoraLinear
+    from dorafactors_b200.parallel import RowShardedDoraLinear
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", 0))
+    try:
+        torch.manual_seed(5)
+        base = torch.nn.Linear(512, 640, bias=True, device="cuda", dtype=torch.bfloat16)
+        ref = DoraLinear(base, r=32, scaling=0.5, init_lora_B_zero=False)
+        sh = RowShardedDoraLinear.from_full(base.weight.detach(), base.bias.detach(), ref.lora_A.weight.detach(),
+                                            ref.lora_B.weight.detach(),
+                                            ref.lora_magnitude_vector.weight.detach(), 0.5)
+        x = torch.randn(96, 512, device="cuda", dtype=torch.bfloat16)
+        dy = torch.randn(96, 640, device="cuda", dtype=torch.bfloat16)
+        x1, x2 = x.clone().requires_grad_(True), x.clone().requires_grad_(True)
+        y1 = ref(x1)
+        y1.backward(dy)
+        y2 = sh(x2)
+        y2.backward(dy)
+        for a, b, k in ((y2, y1, "y"), (x2.grad, x1.grad, "dx"), (sh.lora_A.grad, ref.lora_A.weight.grad, "dA"),
+                        (sh.lora_B.grad, ref.lora_B.weight.grad, "dB"),
+                        (sh.magnitude.grad, ref.lora_magnitude_vector.weight.grad, "dm")):
+            assert_close(to_np(a), to_np(b), 1e-2, k)
+    finally:
+        dist.destroy_process_group()
