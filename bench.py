@@ -248,8 +248,9 @@ def run_native(args) -> None:
 
     def allreduce_grads():
         if world > 1:
-            for p in params:
-                dist.all_reduce(p.grad)
+            from dorafactors_b200.parallel import allreduce_grads as _allreduce
+
+            _allreduce(params)
 
     def step(xin):
         for p in params:
@@ -511,6 +512,90 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_rowshard(args) -> None:
+    """Out-feature row sharding of one 70B-class layer (strong scaling): W0 [out x in]
+    bf16, r = 256, 32768 tokens; every rank holds out/P rows, computes its norm and
+    compose locally and all-gathers the output (one NCCL all-gather per step)."""
+    import datetime
+    import math
+
+    import torch
+    import torch.distributed as dist
+
+    from dorafactors_b200 import _native
+    from dorafactors_b200.parallel import RowShardedDoraLinear
+
+    out_f, in_f = (int(v) for v in args.shape.split("x"))
+    r, T, scale = 256, 32768, 1.0
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29511")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
+                            device_id=device)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device=device).manual_seed(4321)  # identical full tensors on every rank
+    W = (torch.randn(out_f, in_f, device=device, generator=g) * 0.02).bfloat16()
+    A = ((torch.rand(r, in_f, device=device, generator=g) * 2 - 1) / math.sqrt(in_f)).bfloat16()
+    B = (torch.randn(out_f, r, device=device, generator=g) * 0.01).bfloat16()
+    norm = torch.empty(out_f, dtype=torch.bfloat16, device=device)
+    _native.weight_norm(W, A, B, scale, norm)
+    layer = RowShardedDoraLinear.from_full(W, None, A, B, norm.clone(), scale)
+    del W, B
+    x = torch.randn(T, in_f, device=device, generator=g).bfloat16().requires_grad_(True)
+    dy = torch.randn(T, out_f, device=device, generator=g).bfloat16()
+    params = [layer.lora_A, layer.lora_B, layer.magnitude]
+
+    def step():
+        for p_ in params:
+            p_.grad = None
+        x.grad = None
+        y = layer(x)
+        y.backward(dy)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device=device)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms[0])
+    if rank == 0:
+        shard_rows = layer.weight.shape[0]
+        line = {
+            "metric": METRIC,
+            "value": T / (ms * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded normal / uniform weights, normal tokens)",
+            "config": {"workload": f"row-sharded dora_linear_fwd_bwd out={out_f} in={in_f} r={r} tokens={T} bf16",
+                       "out_features": out_f, "in_features": in_f, "rank": r, "tokens": T,
+                       "rows_per_rank": shard_rows, "allgather_bytes_per_step": T * out_f * 2,
+                       "parallelism": f"rowshard{world}"},
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -518,11 +603,16 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core oracle sample")
+    ap.add_argument("--mode", choices=["dp", "rowshard"], default="dp",
+                    help="dp: token data parallelism (default); rowshard: out-feature sharding of one layer")
+    ap.add_argument("--shape", default="28672x8192", help="rowshard mode: out x in of the sharded layer")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "rowshard":
+        run_rowshard(args)
     else:
         run_native(args)
 
