@@ -5,7 +5,9 @@
 //   1. Gram partials   G_z = A[:, Kz] A[:, Kz]^T       tcgen05, split-K, fp32 store
 //   2. Gram reduce     G = sum_z G_z; Y = G^T as fp32 and as a bf16 hi + lo pair
 //   3. cross term      rowsum(B * (W0 A^T)) and ||W0||^2   tcgen05 row-dot, split-K
-//   4. B G B^T term    rowsum(B * (B Y_hi^T + B Y_lo^T))   tcgen05 row-dot
+//   4. B G B^T term    rowsum(B * (B Y_hi^T + B Y_lo^T))   tcgen05 row-dot; for r <= 384
+//                      it runs inside launch 3, each split taking its share of
+//                      G's k-blocks with the B tile already staged in shared memory
 //   5. finalize        fixed-order partial sums + norm assembly + cast
 // fp16 runs step 4 on CUDA cores from the fp32 G (an fp16 hi/lo split could
 // overflow for large Gram entries); every other dtype mix runs steps 1, 3 and
@@ -16,7 +18,7 @@
 namespace dora {
 
 struct NormPlan {
-  bool tc_u, tc_v, tc_g;
+  bool tc_u, tc_v, tc_g, fuse_v;
   int gram_splits, u_splits, u_ntiles, v_splits, v_ntiles;
   size_t off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, total;
 };
@@ -52,7 +54,7 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     const TcGemmShape g = tc_gemm_shape(r, r, in);
     const int64_t tiles = int64_t(g.m_tiles) * g.n_tiles;
     int s = int(sms / (tiles > 0 ? tiles : 1));
-    const int cap = g.kblocks / 8 > 0 ? g.kblocks / 8 : 1;
+    const int cap = g.kblocks / 16 > 0 ? g.kblocks / 16 : 1;
     p.gram_splits = s < 1 ? 1 : (s > cap ? cap : s);
   } else {
     const int64_t tiles = ((r + 63) / 64) * ((r + 63) / 64);
@@ -74,8 +76,12 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     if (s > kb) s = kb;
     p.u_splits = int(s < 1 ? 1 : s);
   }
-  // B G B^T term
-  if (p.tc_v) {
+  // B G B^T term: folded into the cross-term kernel when its tile fits, else its own launch.
+  p.fuse_v = p.tc_u && p.tc_v && tc_can_fuse_v(out, r, in);
+  if (p.fuse_v) {
+    p.v_ntiles = 1;
+    p.v_splits = p.u_splits;
+  } else if (p.tc_v) {
     const TcGemmShape v = tc_gemm_shape(out, r, r);
     p.v_ntiles = v.n_tiles;
     p.v_splits = pick_splits(int64_t(v.m_tiles) * v.n_tiles, 2 * v.kblocks, sms, 4);
@@ -167,6 +173,9 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
     u.dtype = w_dtype; u.X = W; u.Y1 = A; u.Y2 = nullptr; u.Z = B; u.ldz = R;
     u.M = M; u.N = R; u.K = K; u.mode = kGemmRowdot; u.sumsq = true; u.k_splits = p.u_splits;
     u.rowdot_part = cpart; u.sumsq_part = wpart;
+    if (p.fuse_v) {
+      u.G1 = hi; u.G2 = lo; u.v_part = bpart;
+    }
     if ((rc = tc_rowdot_gemm(u, st))) return rc;
   } else {
     simt_gemm<kGemmRowdot, true>(w_dtype, a_dtype, b_dtype, W, K, A, K, B, R, M, R, K, p.u_splits, cpart, wpart,
@@ -174,8 +183,9 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
     if ((rc = check_launch())) return rc;
   }
 
-  // 4. B G B^T term.
-  if (p.tc_v) {
+  // 4. B G B^T term (already done above when fused).
+  if (p.fuse_v) {
+  } else if (p.tc_v) {
     TcGemmArgs v{};
     v.dtype = b_dtype; v.X = B; v.Y1 = hi; v.Y2 = lo; v.Z = B; v.ldz = R;
     v.M = M; v.N = R; v.K = R; v.mode = kGemmRowdot; v.sumsq = false; v.k_splits = p.v_splits;

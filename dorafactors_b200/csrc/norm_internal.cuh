@@ -33,6 +33,12 @@ struct TcGemmArgs {
   float* rowdot_part;        // [n_tiles * k_splits][M]
   float* sumsq_part;         // [k_splits][M]
   float* C;                  // store mode: [k_splits][M][N] fp32
+  // Fused B G B^T phase (rowdot mode, N <= 384): with G1 / G2 = the hi / lo halves of
+  // G^T ([N x N] row-major), every split also adds rowsum(Z * (Z G^T)) over its share
+  // of G's k-blocks into v_part[ks][M].  Requires tc_can_fuse_v(M, N, K).
+  const void* G1 = nullptr;
+  const void* G2 = nullptr;
+  float* v_part = nullptr;
 };
 struct TcGemmShape {
   int nt;        // N tile (columns of TMEM used)
@@ -44,5 +50,6 @@ TcGemmShape tc_gemm_shape(int64_t M, int64_t N, int64_t K);
 bool tc_gemm_supported(int dtype, int64_t M, int64_t N, int64_t K, const void* X, const void* Y, const void* Z,
                        int64_t ldz);
 int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st);
+bool tc_can_fuse_v(int64_t M, int64_t N, int64_t K);
 
 }  // namespace dora
