@@ -13,12 +13,14 @@
 // overflow for large Gram entries); every other dtype mix runs steps 1, 3 and
 // 4 on CUDA cores.  The two-term split keeps about 16 significant bits of G,
 // so B G B^T carries a relative error near 2^-16 instead of bf16's 2^-8.
+#include <cstdlib>
+
 #include "norm_internal.cuh"
 
 namespace dora {
 
 struct NormPlan {
-  bool tc_u, tc_v, tc_g, fuse_v;
+  bool tc_u, tc_v, tc_g, fuse_v, pair_u;
   int gram_splits, u_splits, u_ntiles, v_splits, v_ntiles;
   size_t off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, total;
 };
@@ -42,6 +44,15 @@ static int pick_splits(int64_t tiles, int kb_total, int sms, int max_splits) {
   return best;
 }
 
+// DORA_B200_PAIR=0 selects the single-CTA cross-term kernel (for comparisons).
+static bool use_pair_kernel() {
+  static const bool on = [] {
+    const char* e = std::getenv("DORA_B200_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, int bdt, bool aligned) {
   NormPlan p{};
   const int sms = num_sms();
@@ -63,11 +74,23 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     if (s > kb) s = kb;
     p.gram_splits = int(s < 1 ? 1 : s);
   }
-  // Cross term
+  // Cross term: CTA pairs when the shape allows (half the per-SM operand traffic),
+  // single CTAs otherwise.
+  p.fuse_v = p.tc_u && p.tc_v && tc_can_fuse_v(out, r, in);
   if (p.tc_u) {
     const TcGemmShape u = tc_gemm_shape(out, r, in);
+    TcGemmArgs probe{};
+    probe.mode = kGemmRowdot;
+    probe.Z = reinterpret_cast<const void*>(uintptr_t(256));  // alignment is checked per call
+    probe.ldz = r;
+    probe.M = out;
+    probe.N = r;
+    probe.K = in;
+    if (p.fuse_v) probe.G1 = probe.Z;
+    p.pair_u = use_pair_kernel() && tc2_supported(probe);
     p.u_ntiles = u.n_tiles;
-    p.u_splits = pick_splits(int64_t(u.m_tiles) * u.n_tiles, u.kblocks, sms, 8);
+    p.u_splits = p.pair_u ? pick_splits(int64_t(tc2_pairs(out)) * u.n_tiles, u.kblocks, sms / 2, 8)
+                          : pick_splits(int64_t(u.m_tiles) * u.n_tiles, u.kblocks, sms, 8);
   } else {
     p.u_ntiles = int((r + 63) / 64);
     const int64_t tiles = ((out + 63) / 64) * p.u_ntiles;
@@ -77,7 +100,6 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     p.u_splits = int(s < 1 ? 1 : s);
   }
   // B G B^T term: folded into the cross-term kernel when its tile fits, else its own launch.
-  p.fuse_v = p.tc_u && p.tc_v && tc_can_fuse_v(out, r, in);
   if (p.fuse_v) {
     p.v_ntiles = 1;
     p.v_splits = p.u_splits;
@@ -176,7 +198,10 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
     if (p.fuse_v) {
       u.G1 = hi; u.G2 = lo; u.v_part = bpart;
     }
-    if ((rc = tc_rowdot_gemm(u, st))) return rc;
+    if (p.pair_u && tc2_supported(u)) rc = tc2_rowdot_gemm(u, st);
+    else if (p.pair_u) return DORA_ERR_INVALID_ARGUMENT;  // planned for pairs, but B is misaligned
+    else rc = tc_rowdot_gemm(u, st);
+    if (rc) return rc;
   } else {
     simt_gemm<kGemmRowdot, true>(w_dtype, a_dtype, b_dtype, W, K, A, K, B, R, M, R, K, p.u_splits, cpart, wpart,
                                  nullptr, 0, st);

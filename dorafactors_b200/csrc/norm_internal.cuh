@@ -52,4 +52,10 @@ bool tc_gemm_supported(int dtype, int64_t M, int64_t N, int64_t K, const void* X
 int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st);
 bool tc_can_fuse_v(int64_t M, int64_t N, int64_t K);
 
+// CTA-pair row-dot GEMM (norm_tc2.cu): rowdot mode only, Z row stride 16-byte
+// aligned, M >= 256, N tile <= 512.  Units are pairs of 128-row tiles.
+bool tc2_supported(const TcGemmArgs& a);
+int tc2_pairs(int64_t M);
+int tc2_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st);
+
 }  // namespace dora
