@@ -190,21 +190,13 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+      const MmaChunks chunks = mma_chunks(bf16, nt, BM);
       for (int it = 0; it < iters; ++it) {
         const int s = it % stages, round = it / stages;
         if (!mbar_wait(&full[s], round & 1)) { *aborted = 1; break; }
         tc_fence_after();
         const uint32_t sX = smem_u32(base + size_t(s) * L.stage_bytes);
-        const uint32_t sY = sX + kXTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t adesc = sw128_desc(sX + kk * 32);
-          for (int c0 = 0; c0 < nt; c0 += 256) {
-            const int n = (nt - c0) < 256 ? (nt - c0) : 256;
-            const uint64_t bdesc = sw128_desc(sY + uint32_t(c0) * 128u + kk * 32);
-            umma_f16(tmem_base + uint32_t(c0), adesc, bdesc, make_idesc(bf16, n), (it > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
+        mma_kblock(tmem_base, sX, sX + kXTileBytes, chunks, it > 0);
         umma_commit(&empty[s]);
       }
       bool ok = !*aborted;
@@ -222,15 +214,7 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
           const int kz = kv >= a.v_kblocks ? kv - a.v_kblocks : kv;  // k-block of Z (= column block of B)
           const uint32_t sA = smem_u32(base + size_t(kz) * kXTileBytes);
           const uint32_t sB = smem_u32(base + z_bytes + size_t(vs) * vslot_bytes);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = sw128_desc(sA + kk * 32);
-            for (int c0 = 0; c0 < nt; c0 += 256) {
-              const int n = (nt - c0) < 256 ? (nt - c0) : 256;
-              const uint64_t bdesc = sw128_desc(sB + uint32_t(c0) * 128u + kk * 32);
-              umma_f16(tmem_base + uint32_t(c0), adesc, bdesc, make_idesc(bf16, n), (i > 0 || kk > 0) ? 1u : 0u);
-            }
-          }
+          mma_kblock(tmem_base, sA, sB, chunks, i > 0);
           umma_commit(&vempty[vs]);
         }
         if (ok) umma_commit(vdone);

@@ -46,11 +46,6 @@ inline int pair_stages(int nt) {
   return s > 8 ? 8 : s;
 }
 
-__host__ __device__ constexpr uint32_t make_idesc_pair(bool bf16, int n) {
-  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | (uint32_t(n >> 3) << 17) |
-         (uint32_t(256 >> 4) << 24);
-}
-
 struct PArgs {
   const void* Z;
   int64_t ldz;
@@ -217,21 +212,13 @@ tc2_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+      const MmaChunks chunks = mma_chunks(bf16, nt, 256);
       for (int it = 0; it < iters; ++it) {
         const int s = it % stages, round = it / stages;
         if (!mbar_wait(&full[s], round & 1)) { *aborted = 1; break; }
         tc_fence_after();
         const uint32_t sX = smem_u32(base + size_t(s) * L.stage_bytes);
-        const uint32_t sY = sX + kXTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t adesc = sw128_desc(sX + kk * 32);
-          for (int c0 = 0; c0 < nt; c0 += 256) {
-            const int n = (nt - c0) < 256 ? (nt - c0) : 256;
-            const uint64_t bdesc = sw128_desc(sY + uint32_t(c0 / 2) * 128u + kk * 32);
-            umma2_f16(tmem_base + uint32_t(c0), adesc, bdesc, make_idesc_pair(bf16, n), (it > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
+        mma2_kblock(tmem_base, sX, sX + kXTileBytes, chunks, it > 0);
         umma2_commit_both(&mdone[s]);
       }
       bool ok = !*aborted;
@@ -247,15 +234,7 @@ tc2_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant
           const int kz = kv >= a.v_kblocks ? kv - a.v_kblocks : kv;
           const uint32_t sA = smem_u32(base + size_t(kz) * kXTileBytes);
           const uint32_t sB = smem_u32(base + z_bytes + size_t(vs) * vhalf);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = sw128_desc(sA + kk * 32);
-            for (int c0 = 0; c0 < nt; c0 += 256) {
-              const int n = (nt - c0) < 256 ? (nt - c0) : 256;
-              const uint64_t bdesc = sw128_desc(sB + uint32_t(c0 / 2) * 128u + kk * 32);
-              umma2_f16(tmem_base + uint32_t(c0), adesc, bdesc, make_idesc_pair(bf16, n), (i > 0 || kk > 0) ? 1u : 0u);
-            }
-          }
+          mma2_kblock(tmem_base, sA, sB, chunks, i > 0);
           umma2_commit_both(&vempty[vs]);
         }
         if (ok) umma2_commit_both(vdone);

@@ -171,3 +171,49 @@ def test_norm_full_size_vs_torch_fp32(out_f, in_f, r):
     ref_norm = torch.sqrt((w + 2 * c + b).clamp_min(0)).bfloat16()
     rel = ((norm.float() - ref_norm.float()).abs() / ref_norm.float()).max().item()
     assert rel <= 1e-2
+
+
+_PAIR_SCRIPT = r"""
+import json, sys, torch
+sys.path.insert(0, sys.argv[1])
+from dorafactors_b200 import _native
+out = {}
+for out_f, in_f, r in ((28672, 8192, 384), (8192, 4096, 256), (1000, 2048, 384), (640, 1024, 64)):
+    g = torch.Generator(device="cuda").manual_seed(out_f + r)
+    W = (torch.randn(out_f, in_f, device="cuda", generator=g) * 0.02).bfloat16()
+    A = ((torch.rand(r, in_f, device="cuda", generator=g) * 2 - 1) / in_f**0.5).bfloat16()
+    B = (torch.randn(out_f, r, device="cuda", generator=g) * 0.01).bfloat16()
+    norm = torch.empty(out_f, dtype=torch.bfloat16, device="cuda")
+    parts = torch.empty(3 * out_f, dtype=torch.float32, device="cuda")
+    _native.weight_norm(W, A, B, 1.0, norm, parts)
+    torch.cuda.synchronize()
+    out[f"{out_f}x{in_f}r{r}"] = parts.cpu().tolist()
+out["device_error"] = _native.device_error(reset=True)
+json.dump(out, sys.stdout)
+"""
+
+
+def test_pair_kernel_matches_single():
+    """The CTA-pair (cta_group::2) cross-term kernel, selected by DORA_B200_PAIR=1 in a
+    child process, gives the same fp32 terms as the default single-CTA kernel."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    runs = {}
+    for flag in ("0", "1"):
+        env = dict(os.environ, DORA_B200_PAIR=flag)
+        res = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, root], env=env, capture_output=True, text=True,
+                             timeout=300)
+        assert res.returncode == 0, res.stderr[-2000:]
+        runs[flag] = json.loads(res.stdout)
+    for flag in ("0", "1"):
+        assert runs[flag].pop("device_error") == 0
+    for key, single in runs["0"].items():
+        p = np.asarray(runs["1"][key], np.float64).reshape(3, -1)
+        s = np.asarray(single, np.float64).reshape(3, -1)
+        for i, tol in ((0, 1e-6), (1, 1e-5), (2, 1e-5)):
+            rel = np.linalg.norm(p[i] - s[i]) / max(np.linalg.norm(s[i]), 1e-30)
+            assert rel <= tol, (key, i, rel)
