@@ -147,6 +147,10 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
         for (int j = 0; j * a.ybox < nt; ++j)
           tma_load_2d(sY + size_t(j) * a.ybox * 128, ym, &full[s], kx, int(n0) + j * a.ybox);
         issued = it + 1;
+        // Start this tile's rows of Z on their way into L2 a few k-blocks before the
+        // epilogue stages them, so the staging load after the mainloop hits L2.
+        if (a.z_tma && it == (iters > stages + 1 ? iters - stages - 1 : 0))
+          for (int j = 0; j * BK < nt; ++j) tma_prefetch_2d(&tmZ, int(n0) + j * BK, int(m0));
       }
       if (*aborted) {
         // Let every load this thread issued land before the CTA's shared memory is released.
@@ -256,44 +260,29 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
     // Row dot of the accumulator row with this row of Z: staged Z (64-column boxes,
     // 128-byte rows, 16-byte chunk c of row r stored at c ^ (r % 8)) or global Z.
     auto rowdot_epilogue = [&]() -> float {
-      float acc = 0.f;
-      for (int c0 = 0; c0 < nt; c0 += 32) {
-        if (n0 + c0 >= a.N) break;
-        float v[32];
-        tmem_ld32(trow + uint32_t(c0), v);
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const int64_t ncols = a.N - n0;  // columns of this tile inside N
+      int c0 = 0;
+      // 64 columns per TMEM load while the allocation holds them, then 32.
+      for (; c0 + 64 <= int(a.tmem_cols) && c0 < nt && c0 < ncols; c0 += 64) {
+        float v[64];
+        tmem_ld64(trow + uint32_t(c0), v);
+        const int cnt = (ncols - c0) < 64 ? int(ncols - c0) : 64;
         if (m < a.M) {
-          const int64_t nbase = n0 + c0;
-          const int cnt = (a.N - nbase) < 32 ? int(a.N - nbase) : 32;
-          if (a.z_tma) {
-            const uint8_t* zrow = base + size_t(c0 / BK) * kXTileBytes + row * 128;
-            const int q0 = (c0 % BK) / 8;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 zv = *reinterpret_cast<const uint4*>(zrow + (((q0 + j) ^ (row & 7)) * 16));
-              const T* zh = reinterpret_cast<const T*>(&zv);
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                if (j * 8 + e < cnt) acc = fmaf(v[j * 8 + e], to_f32(zh[e]), acc);
-            }
-          } else {
-            const T* zr = Zg + m * a.ldz + nbase;
-            if (cnt == 32 && ((reinterpret_cast<uintptr_t>(zr) & 15u) == 0)) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 zv = __ldg(reinterpret_cast<const uint4*>(zr) + j);
-                const T* zh = reinterpret_cast<const T*>(&zv);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) acc = fmaf(v[j * 8 + e], to_f32(zh[e]), acc);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < cnt) acc = fmaf(v[j], to_f32(zr[j]), acc);
-            }
-          }
+          if (a.z_tma) dot_staged<T, 64>(v, base, c0, row, cnt, acc);
+          else dot_global<T, 64>(v, Zg + m * a.ldz + n0 + c0, cnt, acc);
         }
       }
-      return acc;
+      for (; c0 < nt && c0 < ncols; c0 += 32) {
+        float v[32];
+        tmem_ld32(trow + uint32_t(c0), v);
+        const int cnt = (ncols - c0) < 32 ? int(ncols - c0) : 32;
+        if (m < a.M) {
+          if (a.z_tma) dot_staged<T, 32>(v, base, c0, row, cnt, acc);
+          else dot_global<T, 32>(v, Zg + m * a.ldz + n0 + c0, cnt, acc);
+        }
+      }
+      return sum8(acc);
     };
     const bool ok = __all_sync(0xffffffffu, !*aborted && mbar_wait(done, 0) && (!a.z_tma || mbar_wait(zfull, 0)));
     if (ok) {

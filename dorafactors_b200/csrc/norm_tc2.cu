@@ -167,6 +167,8 @@ tc2_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant
         tma_load_2d_pair(sX, &tmX, bar_c, kx, int(m0));
         load_half(sX + kXTileBytes, second ? &tmY2 : &tmY1, bar_c, kx, int(n0));
         issued = it + 1;
+        if (a.z_tma && it == (iters > stages + 1 ? iters - stages - 1 : 0))
+          for (int j = 0; j * BK < nt; ++j) tma_prefetch_2d(&tmZ, int(n0) + j * BK, int(m0));
       }
       bool ok = !*aborted;
       if (!ok) {
@@ -273,26 +275,22 @@ tc2_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant
     }
     const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16);
     auto rowdot_epilogue = [&]() -> float {
-      float acc = 0.f;
-      for (int c0 = 0; c0 < nt; c0 += 32) {
-        if (n0 + c0 >= a.N) break;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const int64_t ncols = a.N - n0;
+      int c0 = 0;
+      for (; c0 + 64 <= int(a.tmem_cols) && c0 < nt && c0 < ncols; c0 += 64) {
+        float v[64];
+        tmem_ld64(trow + uint32_t(c0), v);
+        const int cnt = (ncols - c0) < 64 ? int(ncols - c0) : 64;
+        if (m < a.M) dot_staged<T, 64>(v, base, c0, row, cnt, acc);
+      }
+      for (; c0 < nt && c0 < ncols; c0 += 32) {
         float v[32];
         tmem_ld32(trow + uint32_t(c0), v);
-        if (m < a.M) {
-          const int cnt = (a.N - n0 - c0) < 32 ? int(a.N - n0 - c0) : 32;
-          const uint8_t* zrow = base + size_t(c0 / BK) * kXTileBytes + row * 128;
-          const int q0 = (c0 % BK) / 8;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 zv = *reinterpret_cast<const uint4*>(zrow + (((q0 + j) ^ (row & 7)) * 16));
-            const T* zh = reinterpret_cast<const T*>(&zv);
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              if (j * 8 + e < cnt) acc = fmaf(v[j * 8 + e], to_f32(zh[e]), acc);
-          }
-        }
+        const int cnt = (ncols - c0) < 32 ? int(ncols - c0) : 32;
+        if (m < a.M) dot_staged<T, 32>(v, base, c0, row, cnt, acc);
       }
-      return acc;
+      return sum8(acc);
     };
     const bool ok = __all_sync(0xffffffffu, !*aborted && mbar_wait(done, 0) && mbar_wait(zfull, 0));
     if (ok) {

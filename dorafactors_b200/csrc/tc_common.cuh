@@ -100,20 +100,108 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// Load 32 (64) consecutive fp32 accumulator columns of this warp's 32 TMEM lanes
+// (one row per thread).  The wait is part of the same asm statement, so the
+// outputs are defined only once the load has completed.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, "
+      "[%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, "
+      "[%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Prefetch one tile of a tensor map into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
+// Row-dot epilogue pieces: accumulate v[j] * z[j] over NC accumulator columns
+// into eight independent partial sums (one per element of a 16-byte chunk),
+// so the FMA dependence chain is NC / 8 long instead of NC.  Columns at or
+// beyond `cnt` are skipped.
+//
+// Staged Z: 64-column boxes of 128-byte rows, 16-byte chunk c of row r stored
+// at c ^ (r % 8) (the TMA 128-byte swizzle); c0 is a multiple of NC.
+template <typename T, int NC>
+__device__ __forceinline__ void dot_staged(const float (&v)[NC], const uint8_t* ztile, int c0, int row, int cnt,
+                                           float (&acc)[8]) {
+  const uint8_t* zrow = ztile + size_t(c0 / BK) * kXTileBytes + row * 128;
+  const int q0 = (c0 % BK) / 8;
+  if (cnt >= NC) {
+#pragma unroll
+    for (int j = 0; j < NC / 8; ++j) {
+      const uint4 zv = *reinterpret_cast<const uint4*>(zrow + (((q0 + j) ^ (row & 7)) * 16));
+      const T* zh = reinterpret_cast<const T*>(&zv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(v[j * 8 + e], to_f32(zh[e]), acc[e]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NC / 8; ++j) {
+      const uint4 zv = *reinterpret_cast<const uint4*>(zrow + (((q0 + j) ^ (row & 7)) * 16));
+      const T* zh = reinterpret_cast<const T*>(&zv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (j * 8 + e < cnt) acc[e] = fmaf(v[j * 8 + e], to_f32(zh[e]), acc[e]);
+    }
+  }
+}
+// Z row read from global memory (zr points at column c0 of this thread's row).
+template <typename T, int NC>
+__device__ __forceinline__ void dot_global(const float (&v)[NC], const T* zr, int cnt, float (&acc)[8]) {
+  if (cnt >= NC && (reinterpret_cast<uintptr_t>(zr) & 15u) == 0) {
+#pragma unroll
+    for (int j = 0; j < NC / 8; ++j) {
+      const uint4 zv = __ldg(reinterpret_cast<const uint4*>(zr) + j);
+      const T* zh = reinterpret_cast<const T*>(&zv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(v[j * 8 + e], to_f32(zh[e]), acc[e]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NC; ++j)
+      if (j < cnt) acc[j & 7] = fmaf(v[j], to_f32(zr[j]), acc[j & 7]);
+  }
+}
+__device__ __forceinline__ float sum8(const float (&acc)[8]) {
+  return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
 }
 
 
