@@ -4,7 +4,8 @@
 // Launches (tensor-core path, bf16 weights and adapters):
 //   1. Gram partials   G_z = A[:, Kz] A[:, Kz]^T       tcgen05, split-K, fp32 store
 //   2. Gram reduce     G = sum_z G_z; Y = G^T as fp32 and as a bf16 hi + lo pair
-//   3. cross term      rowsum(B * (W0 A^T)) and ||W0||^2   tcgen05 row-dot, split-K
+//   3. cross term      rowsum(B * (W0 A^T)) and ||W0||^2   tcgen05 row-dot, stream-K
+//                      (one CTA per SM, equal shares of all tiles' k-blocks)
 //   4. B G B^T term    rowsum(B * (B Y_hi^T + B Y_lo^T))   tcgen05 row-dot; for r <= 384
 //                      it runs inside launch 3, each split taking its share of
 //                      G's k-blocks with the B tile already staged in shared memory
@@ -20,7 +21,8 @@
 namespace dora {
 
 struct NormPlan {
-  bool tc_u, tc_v, tc_g, fuse_v, pair_u;
+  bool tc_u, tc_v, tc_g, fuse_v, pair_u, sk_u;
+  SkPlan sk;
   int gram_splits, u_splits, u_ntiles, v_splits, v_ntiles;
   size_t off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, total;
 };
@@ -55,6 +57,15 @@ static bool use_pair_kernel() {
   return on;
 }
 
+// DORA_B200_SK=0 selects the split-K cross-term kernel instead of the stream-K one.
+static bool use_sk_kernel() {
+  static const bool on = [] {
+    const char* e = std::getenv("DORA_B200_SK");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, int bdt, bool aligned) {
   NormPlan p{};
   const int sms = num_sms();
@@ -67,7 +78,10 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     const TcGemmShape g = tc_gemm_shape(r, r, in);
     const int64_t tiles = int64_t(g.m_tiles) * g.n_tiles;
     int s = int(sms / (tiles > 0 ? tiles : 1));
-    const int cap = g.kblocks / 16 > 0 ? g.kblocks / 16 : 1;
+    // At least 4 (one output tile) or 8 k-blocks per split: each split's partial tile is
+    // re-read by the reduce, and a split shorter than the pipeline depth only adds latency.
+    const int per = tiles == 1 ? 4 : 8;
+    const int cap = g.kblocks / per > 0 ? g.kblocks / per : 1;
     p.gram_splits = s < 1 ? 1 : (s > cap ? cap : s);
   } else {
     const int64_t tiles = ((r + 63) / 64) * ((r + 63) / 64);
@@ -88,11 +102,22 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     probe.M = out;
     probe.N = r;
     probe.K = in;
-    if (p.fuse_v) probe.G1 = probe.Z;
+    probe.sumsq = true;
+    if (p.fuse_v) {
+      probe.G1 = probe.Z;
+      probe.G2 = probe.Z;
+      probe.v_part = reinterpret_cast<float*>(uintptr_t(256));
+    }
     p.pair_u = use_pair_kernel() && tc2_supported(probe);
+    p.sk_u = !p.pair_u && use_sk_kernel() && tc_sk_supported(probe);
     p.u_ntiles = u.n_tiles;
-    p.u_splits = p.pair_u ? pick_splits(int64_t(tc2_pairs(out)) * u.n_tiles, u.kblocks, sms / 2, 8)
-                          : pick_splits(int64_t(u.m_tiles) * u.n_tiles, u.kblocks, sms, 8);
+    if (p.sk_u) {
+      p.sk = tc_sk_plan(out, r, in, p.fuse_v, sms);
+      p.u_splits = p.sk.slots;
+    } else {
+      p.u_splits = p.pair_u ? pick_splits(int64_t(tc2_pairs(out)) * u.n_tiles, u.kblocks, sms / 2, 8)
+                            : pick_splits(int64_t(u.m_tiles) * u.n_tiles, u.kblocks, sms, 8);
+    }
   } else {
     p.u_ntiles = int((r + 63) / 64);
     const int64_t tiles = ((out + 63) / 64) * p.u_ntiles;
@@ -202,6 +227,8 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
     }
     if (p.pair_u && tc2_supported(u)) rc = tc2_rowdot_gemm(u, st);
     else if (p.pair_u) return DORA_ERR_INVALID_ARGUMENT;  // planned for pairs, but B is misaligned
+    else if (p.sk_u && tc_sk_supported(u)) rc = tc_sk_rowdot_gemm(u, p.sk, st);
+    else if (p.sk_u) return DORA_ERR_INVALID_ARGUMENT;
     else rc = tc_rowdot_gemm(u, st);
     if (rc) return rc;
   } else {

@@ -58,4 +58,17 @@ bool tc2_supported(const TcGemmArgs& a);
 int tc2_pairs(int64_t M);
 int tc2_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st);
 
+// Stream-K row-dot kernel (norm_sk.cu): rowdot mode with the ||X||^2 row sums, one
+// N tile (N <= 512), Z row stride 16-byte aligned, no Y2; optionally the fused
+// B G B^T phase (G1 / G2 / v_part, tc_can_fuse_v).  The units of all tiles are
+// split evenly over `grid` CTAs; partial slot s of a row comes from the s-th CTA
+// that touches its tile, so rowdot_part, sumsq_part and v_part are [slots][M].
+struct SkPlan {
+  int grid, slots;
+  int64_t units_per_tile, total_units;
+};
+bool tc_sk_supported(const TcGemmArgs& a);
+SkPlan tc_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms);
+int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st);
+
 }  // namespace dora

@@ -1,0 +1,500 @@
+// Stream-K form of the tensor-core row-dot kernel for the factored norm's cross
+// term (with the fused B G B^T phase and ||W0||^2).
+//
+// The work of one 128-row tile is a row of "units": its kb_total k-blocks of
+// X Y^T (W0 A^T) followed, when the B G B^T phase is fused, by its 2 x
+// ceil(N / 64) k-blocks of Z G^T (B times the hi and lo halves of G).  Both kinds
+// cost one 128 x NT x 64 MMA block.  The units of all tiles, tile after tile, are
+// cut into `grid` equal contiguous ranges, one per CTA (one CTA per SM), so every
+// SM gets the same amount of MMA work whatever the tile count, and a CTA pays
+// its prologue (barrier set-up, TMEM allocation, pipeline fill) once.
+//
+// A CTA's range crosses at most a few tile boundaries; the part of the range
+// inside one tile is a "segment".  Per segment:
+//   mainloop   TMA ring of X / Y stages, tcgen05.mma into TMEM (fp32), row
+//              warps sum the squares of the staged X rows (||W0||^2);
+//   staging    once the ring is idle, the tile's Z rows (B) come into it through
+//              TMA, then the G k-blocks of the segment double-buffered behind it;
+//   epilogue   rowsum(acc * Z) for the segment's X Y^T units, then the segment's
+//              Z G^T units accumulate in the same TMEM columns and are contracted
+//              the same way.
+// Segment s of a tile (s = 0 for the CTA that starts the tile) writes partial
+// slot s of each row; the slots a tile does not use are zero-filled by its
+// slot-0 segment, so the finalize kernel sums a fixed number of slots in a fixed
+// order (the result is deterministic for a given grid size).
+//
+// Every mbarrier wait is bounded (about a second); on expiry the kernel records
+// DORA_ERR_DEVICE_TIMEOUT, stops issuing work, drains what it issued and
+// returns.  No cluster, no multicast.
+#include <atomic>
+#include <type_traits>
+
+#include "tc_common.cuh"
+
+namespace dora {
+namespace tc {
+
+// Units [sk_begin(c), sk_begin(c + 1)) belong to CTA c.
+__host__ __device__ inline int64_t sk_begin(int64_t c, int64_t total, int64_t grid) { return c * total / grid; }
+// The CTA whose range holds unit x.
+__host__ __device__ inline int64_t sk_owner(int64_t x, int64_t total, int64_t grid) {
+  int64_t c = x * grid / total;
+  while (c + 1 < grid && sk_begin(c + 1, total, grid) <= x) ++c;
+  while (c > 0 && sk_begin(c, total, grid) > x) --c;
+  return c;
+}
+
+struct SkArgs {
+  int64_t M, N;
+  int nt, ybox, m_tiles, kblocks, stages, grid, slots;
+  int apart;           // Z and the G slots have their own region after the ring (else they reuse the ring)
+  uint32_t stage_off;  // Z / G region, from the 1024-aligned base
+  uint32_t bar_off;    // barriers, from the 1024-aligned base
+  int fuse_v, v_kblocks;
+  int64_t units_per_tile, total_units;
+  uint32_t tmem_cols;
+  float* rowdot_part;  // [slots][M]
+  float* sumsq_part;   // [slots][M]
+  float* v_part;       // [slots][M] when fuse_v
+};
+
+__host__ __device__ inline uint32_t sk_stage_bytes(int nt) { return kXTileBytes + uint32_t(nt) * 128u; }
+
+// Shared-memory layout: a ring of `stages` X / Y stages, then (when the tile is
+// narrow enough) a separate region for the staged Z rows and two G slots, so
+// the next segment's ring loads can stream in while this segment's epilogue
+// runs; wide tiles stage Z / G in the idle ring instead.
+struct SkLayout {
+  int stages, apart;
+  uint32_t stage_off, bar_off, total;
+};
+inline SkLayout sk_layout(int nt, bool fuse_v) {
+  const uint32_t budget = 220u * 1024u;
+  const uint32_t stage = sk_stage_bytes(nt);
+  const uint32_t z_bytes = uint32_t((nt + BK - 1) / BK) * kXTileBytes;
+  const uint32_t staging = z_bytes + (fuse_v ? 2u * uint32_t(nt) * 128u : 0u);
+  SkLayout L{};
+  int s_apart = staging < budget ? int((budget - staging) / stage) : 0;
+  if (s_apart > 8) s_apart = 8;
+  if (s_apart >= 4) {
+    L.stages = s_apart;
+    L.apart = 1;
+    L.stage_off = stage * uint32_t(s_apart);
+    L.bar_off = L.stage_off + staging;
+  } else {
+    int s = int(budget / stage);
+    L.stages = s > 8 ? 8 : s;
+    L.apart = 0;
+    L.stage_off = 0;
+    L.bar_off = stage * uint32_t(L.stages);
+  }
+  L.total = 1024u + L.bar_off + 256u;
+  return L;
+}
+
+template <typename T, bool kSumSq>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY,
+                    const __grid_constant__ CUtensorMap tmZ, const __grid_constant__ CUtensorMap tmG1,
+                    const __grid_constant__ CUtensorMap tmG2, const SkArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nt = a.nt, S = a.stages;
+  const uint32_t stage_bytes = sk_stage_bytes(nt);
+  uint8_t* zbase = base + a.stage_off;  // staged Z rows, then two G slots
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + a.bar_off);
+  uint64_t* empty = full + S;
+  uint64_t* done = empty + S;       // MMA -> rows: the segment's X Y^T units are accumulated
+  uint64_t* zfull = done + 1;       // producer -> all: the segment's Z rows are staged
+  uint64_t* vfull = zfull + 1;      // [2] G k-block slots
+  uint64_t* vempty = vfull + 2;     // [2]
+  uint64_t* tmem_free = vempty + 2; // rows -> MMA: first epilogue done with TMEM
+  uint64_t* vdone = tmem_free + 1;  // MMA -> rows: the segment's Z G^T units are accumulated
+  uint64_t* seg_free = vdone + 1;   // rows -> producer, MMA: TMEM and staged Z no longer read
+  uint64_t* drain = seg_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* aborted = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = blockIdx.x;
+  const int64_t TU = a.units_per_tile, TOT = a.total_units, G = a.grid;
+  const int kbt = a.kblocks;  // X Y^T units per tile; the rest of a tile's units are Z G^T
+  const int vkb = a.v_kblocks;
+  const int nzb = (nt + BK - 1) / BK;
+  const uint32_t z_bytes = uint32_t(nzb) * kXTileBytes;
+  const uint32_t vslot_bytes = uint32_t(nt) * 128u;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + (kSumSq ? 4 : 0));
+    }
+    mbar_init(done, 1);
+    mbar_init(zfull, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&vfull[s], 1);
+      mbar_init(&vempty[s], 1);
+    }
+    mbar_init(tmem_free, 4);
+    mbar_init(vdone, 1);
+    mbar_init(seg_free, 4);
+    mbar_init(drain, 1);
+    *aborted = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(a.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t u_first = sk_begin(c, TOT, G), u_last = sk_begin(c + 1, TOT, G);
+  // Segment `seg` of this CTA: tile, tile-local unit range [ua, ub), its X Y^T
+  // part [ua, min(ub, kbt)) and its Z G^T part [max(ua, kbt), ub) - kbt.
+  struct Seg {
+    int64_t tile;
+    int ua, ub, u_iters, v0, v_iters;
+  };
+  auto segment = [&](int64_t u) {
+    Seg s;
+    s.tile = u / TU;
+    s.ua = int(u - s.tile * TU);
+    const int64_t e = u_last - s.tile * TU;
+    s.ub = int(e < TU ? e : TU);
+    const int xe = s.ub < kbt ? s.ub : kbt;
+    s.u_iters = xe > s.ua ? xe - s.ua : 0;
+    s.v0 = (s.ua > kbt ? s.ua : kbt) - kbt;
+    s.v_iters = s.ub - kbt - s.v0 > 0 ? s.ub - kbt - s.v0 : 0;
+    return s;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmY)) : "memory");
+      int64_t gk = 0, gv = 0;  // ring uses and G slot uses so far
+      int z_seg = -1;  // segment whose Z staging load this thread issued last
+      int seg = 0;
+      for (int64_t u = u_first; u < u_last && !*aborted; ++seg) {
+        const Seg sg = segment(u);
+        u = sg.tile * TU + sg.ub;
+        const int m0 = int(sg.tile * BM);
+        // Ring mode: the previous segment's epilogues must be done with the staged Z / G
+        // (which live in the ring) before the ring is refilled.
+        if (!a.apart && seg > 0 && !mbar_wait(seg_free, (seg - 1) & 1)) { *aborted = 1; break; }
+        for (int i = 0; i < sg.u_iters; ++i) {
+          const int64_t g = gk;
+          const int s = int(g % S);
+          if (g >= S && !mbar_wait(&empty[s], uint32_t((g / S - 1) & 1))) { *aborted = 1; break; }
+          if (*aborted) break;
+          const int kx = (sg.ua + i) * BK;
+          uint8_t* sX = base + size_t(s) * stage_bytes;
+          mbar_expect_tx(&full[s], stage_bytes);
+          tma_load_2d(sX, &tmX, &full[s], kx, m0);
+          for (int j = 0; j * a.ybox < nt; ++j)
+            tma_load_2d(sX + kXTileBytes + size_t(j) * a.ybox * 128, &tmY, &full[s], kx, j * a.ybox);
+          ++gk;
+          // Start the tile's Z rows towards L2 a few k-blocks before they are staged.
+          if (i == (sg.u_iters > S + 1 ? sg.u_iters - S - 1 : 0))
+            for (int j = 0; j < nzb; ++j) tma_prefetch_2d(&tmZ, j * BK, m0);
+        }
+        if (*aborted) break;
+        bool ok = true;
+        if (a.apart) {
+          // Own region: only the previous segment's epilogues have to be done with it.
+          if (seg > 0) ok = mbar_wait(seg_free, (seg - 1) & 1);
+        } else {
+          // Ring idle: every issued X / Y stage has been consumed by the MMAs (and the row sums).
+          for (int64_t g = gk - S > 0 ? gk - S : 0; g < gk && ok; ++g)
+            ok = mbar_wait(&empty[g % S], uint32_t((g / S) & 1));
+        }
+        if (!ok) { *aborted = 1; break; }
+        mbar_expect_tx(zfull, z_bytes);
+        for (int j = 0; j < nzb; ++j) tma_load_2d(zbase + size_t(j) * kXTileBytes, &tmZ, zfull, j * BK, m0);
+        z_seg = seg;
+        for (int i = 0; i < sg.v_iters; ++i) {
+          const int64_t g = gv;
+          const int vs = int(g & 1);
+          if (g >= 2 && !mbar_wait(&vempty[vs], uint32_t((g / 2 - 1) & 1))) { *aborted = 1; break; }
+          const int kv = sg.v0 + i;
+          const bool lo = kv >= vkb;
+          const int kx = (lo ? kv - vkb : kv) * BK;
+          uint8_t* slot = zbase + z_bytes + size_t(vs) * vslot_bytes;
+          mbar_expect_tx(&vfull[vs], vslot_bytes);
+          const CUtensorMap* gm = lo ? &tmG2 : &tmG1;
+          for (int j = 0; j * a.ybox < nt; ++j)
+            tma_load_2d(slot + size_t(j) * a.ybox * 128, gm, &vfull[vs], kx, j * a.ybox);
+          ++gv;
+        }
+      }
+      // Let every copy this thread issued land before the CTA's shared memory goes away.
+      for (int64_t g = gk - S > 0 ? gk - S : 0; g < gk; ++g) mbar_wait(&full[g % S], uint32_t((g / S) & 1));
+      if (z_seg >= 0) mbar_wait(zfull, uint32_t(z_seg & 1));
+      for (int64_t g = gv - 2 > 0 ? gv - 2 : 0; g < gv; ++g) mbar_wait(&vfull[g & 1], uint32_t((g / 2) & 1));
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+      const MmaChunks chunks = mma_chunks(bf16, nt, BM);
+      int64_t gk = 0, gv = 0;
+      int n_tf = 0;  // tmem_free phases consumed
+      int seg = 0;
+      bool ok = true;
+      for (int64_t u = u_first; u < u_last && ok; ++seg) {
+        const Seg sg = segment(u);
+        u = sg.tile * TU + sg.ub;
+        if (seg > 0 && !mbar_wait(seg_free, (seg - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        for (int i = 0; i < sg.u_iters; ++i) {
+          const int64_t g = gk++;
+          const int s = int(g % S);
+          if (!mbar_wait(&full[s], uint32_t((g / S) & 1))) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sX = smem_u32(base + size_t(s) * stage_bytes);
+          mma_kblock(tmem_base, sX, sX + kXTileBytes, chunks, i > 0);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        if (sg.u_iters > 0) umma_commit(done);
+        if (sg.v_iters > 0) {
+          if (!mbar_wait(zfull, seg & 1)) { ok = false; break; }
+          if (sg.u_iters > 0) {
+            if (!mbar_wait(tmem_free, n_tf & 1)) { ok = false; break; }
+            ++n_tf;
+          }
+          tc_fence_after();
+          for (int i = 0; i < sg.v_iters; ++i) {
+            const int64_t g = gv++;
+            const int vs = int(g & 1);
+            if (!mbar_wait(&vfull[vs], uint32_t((g / 2) & 1))) { ok = false; break; }
+            tc_fence_after();
+            const int kv = sg.v0 + i;
+            const int kz = kv >= vkb ? kv - vkb : kv;  // k-block of Z (= column block of B)
+            const uint32_t sA = smem_u32(zbase + size_t(kz) * kXTileBytes);
+            const uint32_t sB = smem_u32(zbase + z_bytes + size_t(vs) * vslot_bytes);
+            mma_kblock(tmem_base, sA, sB, chunks, i > 0);
+            umma_commit(&vempty[vs]);
+          }
+          if (!ok) break;
+          umma_commit(vdone);
+        }
+      }
+      if (!ok) *aborted = 1;
+      umma_commit(drain);  // completes once every MMA issued above has finished
+      mbar_wait(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ row threads
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16);
+    auto rowdot_epilogue = [&]() -> float {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const int64_t ncols = a.N;
+      int c0 = 0;
+      for (; c0 + 64 <= int(a.tmem_cols) && c0 < nt && c0 < ncols; c0 += 64) {
+        float v[64];
+        tmem_ld64(trow + uint32_t(c0), v);
+        const int cnt = (ncols - c0) < 64 ? int(ncols - c0) : 64;
+        dot_staged<T, 64>(v, zbase, c0, row, cnt, acc);
+      }
+      for (; c0 < nt && c0 < ncols; c0 += 32) {
+        float v[32];
+        tmem_ld32(trow + uint32_t(c0), v);
+        const int cnt = (ncols - c0) < 32 ? int(ncols - c0) : 32;
+        dot_staged<T, 32>(v, zbase, c0, row, cnt, acc);
+      }
+      return sum8(acc);
+    };
+    int64_t gk = 0;
+    int n_done = 0, n_vdone = 0;
+    int seg = 0;
+    for (int64_t u = u_first; u < u_last; ++seg) {
+      const Seg sg = segment(u);
+      u = sg.tile * TU + sg.ub;
+      const int64_t m = sg.tile * BM + row;
+      float ssq = 0.f;
+      bool ok = true;
+      if (kSumSq) {
+        for (int i = 0; i < sg.u_iters; ++i) {
+          const int64_t g = gk++;
+          const int s = int(g % S);
+          if (!__all_sync(0xffffffffu, mbar_wait(&full[s], uint32_t((g / S) & 1)))) { ok = false; break; }
+          const uint8_t* rowp = base + size_t(s) * stage_bytes + row * 128;
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            // Rotate the 16-byte chunk order by lane so a quarter-warp touches 8 distinct bank groups.
+            const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((p + lane) & 7) * 16);
+            const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float x = to_f32(h[e]);
+              ssq = fmaf(x, x, ssq);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        }
+      }
+      const int64_t first = sk_owner(sg.tile * TU, TOT, G);
+      const int slot = int(c - first);
+      ok = ok && __all_sync(0xffffffffu, !*aborted && mbar_wait(zfull, seg & 1) &&
+                                             (sg.u_iters == 0 || mbar_wait(done, n_done & 1)));
+      if (!ok) {
+        *aborted = 1;
+        break;
+      }
+      if (sg.u_iters > 0) ++n_done;
+      tc_fence_after();
+      const float cacc = sg.u_iters > 0 ? rowdot_epilogue() : 0.f;
+      if (m < a.M) {
+        a.rowdot_part[int64_t(slot) * a.M + m] = cacc;
+        a.sumsq_part[int64_t(slot) * a.M + m] = ssq;
+      }
+      float bacc = 0.f;
+      if (sg.v_iters > 0) {
+        if (sg.u_iters > 0) {
+          // Hand the TMEM columns to the Z G^T units.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tmem_free);
+        }
+        if (!__all_sync(0xffffffffu, !*aborted && mbar_wait(vdone, n_vdone & 1))) {
+          *aborted = 1;
+          break;
+        }
+        ++n_vdone;
+        tc_fence_after();
+        bacc = rowdot_epilogue();
+      }
+      if (a.fuse_v && m < a.M) a.v_part[int64_t(slot) * a.M + m] = bacc;
+      if (slot == 0 && m < a.M) {
+        // Zero the slots this tile does not use, so the finalize sums a fixed count.
+        const int used = int(sk_owner(sg.tile * TU + TU - 1, TOT, G) - first) + 1;
+        for (int s2 = used; s2 < a.slots; ++s2) {
+          a.rowdot_part[int64_t(s2) * a.M + m] = 0.f;
+          a.sumsq_part[int64_t(s2) * a.M + m] = 0.f;
+          if (a.fuse_v) a.v_part[int64_t(s2) * a.M + m] = 0.f;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(seg_free);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(a.tmem_cols)
+                 : "memory");
+  }
+}
+
+
+}  // namespace tc
+
+bool tc_sk_supported(const TcGemmArgs& a) {
+  if (a.mode != kGemmRowdot || !a.sumsq || a.Y2 || !a.Z || a.ldz != a.N || (a.ldz * 2) % 16 != 0 ||
+      !aligned16(a.Z))
+    return false;
+  const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K);
+  if (sh.n_tiles != 1) return false;
+  const tc::SkLayout L = tc::sk_layout(sh.nt, a.G1 != nullptr);
+  const uint32_t z_bytes = uint32_t((sh.nt + tc::BK - 1) / tc::BK) * tc::kXTileBytes;
+  const uint32_t staging = z_bytes + (a.G1 ? 2u * uint32_t(sh.nt) * 128u : 0u);
+  if (L.stages < 2 || (!L.apart && staging > L.bar_off)) return false;
+  if (a.G1 && (!a.G2 || !a.v_part || !tc_can_fuse_v(a.M, a.N, a.K))) return false;
+  return true;
+}
+
+SkPlan tc_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
+  const TcGemmShape sh = tc_gemm_shape(M, N, K);
+  SkPlan p;
+  p.units_per_tile = int64_t(sh.kblocks) + (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
+  p.total_units = int64_t(sh.m_tiles) * p.units_per_tile;
+  // One CTA per SM, but no CTA with fewer than four units (each segment pays a staging and epilogue).
+  int64_t g = p.total_units / 4;
+  if (g > sms) g = sms;
+  if (g < 1) g = 1;
+  p.grid = int(g);
+  int slots = 1;
+  for (int64_t t = 0; t < sh.m_tiles; ++t) {
+    const int64_t f = tc::sk_owner(t * p.units_per_tile, p.total_units, g);
+    const int64_t l = tc::sk_owner(t * p.units_per_tile + p.units_per_tile - 1, p.total_units, g);
+    if (int(l - f + 1) > slots) slots = int(l - f + 1);
+  }
+  p.slots = slots;
+  return p;
+}
+
+template <typename T, bool SSQ>
+static int launch_sk(const tc::SkArgs& k, const CUtensorMap* m, cudaStream_t st) {
+  const uint32_t smem = 1024u + k.bar_off + 256u;
+  auto kfn = tc::tc_sk_rowdot_kernel<T, SSQ>;
+  static std::atomic<unsigned long long> opted{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(opted.load(std::memory_order_relaxed) & bit)) {
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tc::kMaxDynamicSmem));
+    if (e != cudaSuccess) return set_cuda_error(e);
+    opted.fetch_or(bit, std::memory_order_relaxed);
+  }
+  kfn<<<unsigned(k.grid), tc::kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], k);
+  return check_launch();
+}
+
+int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
+  if (!tc_sk_supported(a)) return DORA_ERR_UNSUPPORTED;
+  const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K);
+  const int ybox = sh.nt <= 256 ? sh.nt : 128;
+  const bool fuse = a.G1 != nullptr;
+  CUtensorMap maps[5];
+  if (!tc::make_map(&maps[0], a.X, a.dtype, a.M, a.K, tc::BM) || !tc::make_map(&maps[1], a.Y1, a.dtype, a.N, a.K, ybox) ||
+      !tc::make_map(&maps[2], a.Z, a.dtype, a.M, a.ldz, tc::BM))
+    return DORA_ERR_CUDA;
+  maps[3] = maps[1];
+  maps[4] = maps[1];
+  if (fuse && (!tc::make_map(&maps[3], a.G1, a.dtype, a.N, a.N, ybox) ||
+               !tc::make_map(&maps[4], a.G2, a.dtype, a.N, a.N, ybox)))
+    return DORA_ERR_CUDA;
+  tc::SkArgs k{};
+  k.M = a.M;
+  k.N = a.N;
+  k.nt = sh.nt;
+  k.ybox = ybox;
+  k.m_tiles = sh.m_tiles;
+  k.kblocks = sh.kblocks;
+  const tc::SkLayout L = tc::sk_layout(sh.nt, fuse);
+  k.stages = L.stages;
+  k.apart = L.apart;
+  k.stage_off = L.stage_off;
+  k.bar_off = L.bar_off;
+  k.grid = p.grid;
+  k.slots = p.slots;
+  k.fuse_v = fuse ? 1 : 0;
+  k.v_kblocks = int((a.N + tc::BK - 1) / tc::BK);
+  k.units_per_tile = int64_t(sh.kblocks) + (fuse ? 2 * k.v_kblocks : 0);
+  k.total_units = int64_t(sh.m_tiles) * k.units_per_tile;
+  if (k.units_per_tile != p.units_per_tile || k.total_units != p.total_units) return DORA_ERR_INVALID_ARGUMENT;
+  uint32_t cols = 32;
+  while (cols < uint32_t(sh.nt)) cols <<= 1;
+  k.tmem_cols = cols;
+  k.rowdot_part = a.rowdot_part;
+  k.sumsq_part = a.sumsq_part;
+  k.v_part = a.v_part;
+  if (a.dtype == DORA_DTYPE_BF16) return launch_sk<__nv_bfloat16, true>(k, maps, st);
+  return launch_sk<__half, true>(k, maps, st);
+}
+
+}  // namespace dora

@@ -58,6 +58,18 @@ struct PArgs {
   float* v_part;
 };
 
+// Tile row (= column of A, G and Z) held in accumulator column c when each CTA of
+// the pair stages one contiguous half of the tile's B-operand rows: chunk 0
+// (N0 = min(nt, 256) columns) takes rows [0, N0/2) from CTA 0 and [nt/2, nt/2 +
+// N0/2) from CTA 1; chunk 1 (nt - N0 columns) takes the next rows of each half.
+// The identity for nt <= 256; a swap of 64-column-aligned blocks for nt = 384, 512.
+__host__ __device__ inline int pair_col_row(int c, int nt) {
+  const int n0 = nt < 256 ? nt : 256, h0 = n0 / 2, half = nt / 2;
+  if (c < n0) return c < h0 ? c : half + (c - h0);
+  const int i = c - n0, h1 = (nt - n0) / 2;
+  return i < h1 ? h0 + i : half + h0 + (i - h1);
+}
+
 template <typename T, bool kSumSq>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 tc2_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY1,
@@ -135,16 +147,13 @@ tc2_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  // Y (and G) halves: for each MMA chunk of up to 256 columns this CTA stages
-  // rows [c0 + rank * n/2, c0 + (rank + 1) * n/2) at offset (c0 / 2) rows.
+  // Y (and G) halves: CTA r stages rows [r * nt/2, (r + 1) * nt/2) of the tile as
+  // one box.  Its first N0/2 rows (N0 = min(nt, 256)) are its half of MMA chunk 0,
+  // the rest its half of chunk 1, so accumulator column c holds tile row
+  // pair_col_row(c, nt) -- a permutation of 64-column blocks that the epilogue
+  // undoes when it picks the matching Z columns.
   auto load_half = [&](uint8_t* dst, const CUtensorMap* map, uint32_t bar_c, int kx, int row_base) {
-    for (int c0 = 0; c0 < nt; c0 += 256) {
-      const int n = (nt - c0) < 256 ? (nt - c0) : 256;
-      const int half = n / 2;
-      uint8_t* d = dst + size_t(c0 / 2) * 128;
-      for (int j = 0; j * a.hb < half; ++j)
-        tma_load_2d_pair(d + size_t(j) * a.hb * 128, map, bar_c, kx, row_base + c0 + int(rank) * half + j * a.hb);
-    }
+    tma_load_2d_pair(dst, map, bar_c, kx, row_base + int(rank) * (nt / 2));
   };
 
   if (warp == 0) {
@@ -278,17 +287,21 @@ tc2_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       const int64_t ncols = a.N - n0;
       int c0 = 0;
-      for (; c0 + 64 <= int(a.tmem_cols) && c0 < nt && c0 < ncols; c0 += 64) {
+      for (; c0 + 64 <= int(a.tmem_cols) && c0 < nt; c0 += 64) {
+        const int zc = pair_col_row(c0, nt);  // 64-column blocks map to contiguous Z columns
+        if (zc >= ncols) continue;            // warp-uniform: the TMEM load is skipped by all lanes
         float v[64];
         tmem_ld64(trow + uint32_t(c0), v);
-        const int cnt = (ncols - c0) < 64 ? int(ncols - c0) : 64;
-        if (m < a.M) dot_staged<T, 64>(v, base, c0, row, cnt, acc);
+        const int cnt = (ncols - zc) < 64 ? int(ncols - zc) : 64;
+        if (m < a.M) dot_staged<T, 64>(v, base, zc, row, cnt, acc);
       }
-      for (; c0 < nt && c0 < ncols; c0 += 32) {
+      for (; c0 < nt; c0 += 32) {  // allocations of 32 columns (nt <= 32: identity order)
+        const int zc = pair_col_row(c0, nt);
+        if (zc >= ncols) continue;
         float v[32];
         tmem_ld32(trow + uint32_t(c0), v);
-        const int cnt = (ncols - c0) < 32 ? int(ncols - c0) : 32;
-        if (m < a.M) dot_staged<T, 32>(v, base, c0, row, cnt, acc);
+        const int cnt = (ncols - zc) < 32 ? int(ncols - zc) : 32;
+        if (m < a.M) dot_staged<T, 32>(v, base, zc, row, cnt, acc);
       }
       return sum8(acc);
     };
@@ -369,7 +382,7 @@ int tc2_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st) {
   const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K);
   const int kb_total = a.Y2 ? 2 * sh.kblocks : sh.kblocks;
   if (a.k_splits < 1 || a.k_splits > kb_total) return DORA_ERR_INVALID_ARGUMENT;
-  const int hb = sh.nt <= 256 ? sh.nt / 2 : 64;
+  const int hb = sh.nt / 2;  // one box per CTA half (nt <= 512, so at most 256 rows)
   CUtensorMap maps[6];
   if (!tc::make_map(&maps[0], a.X, a.dtype, a.M, a.K, tc::BM) || !tc::make_map(&maps[1], a.Y1, a.dtype, a.N, a.K, hb) ||
       !tc::make_map(&maps[2], a.Y2 ? a.Y2 : a.Y1, a.dtype, a.N, a.K, hb) ||

@@ -3,6 +3,7 @@
     python -m dorafactors_b200.microbench --op norm --out 8192 --in 8192 --rank 384
     python -m dorafactors_b200.microbench --op compose_fwd --rows 16384 --cols 28672
     python -m dorafactors_b200.microbench --op compose_bwd --rows 16384 --cols 28672
+    python -m dorafactors_b200.microbench --op linear_output_bwd --rows 16384 --cols 28672
     python -m dorafactors_b200.microbench --op sweep      # rank sweep on an 8192 x 8192 layer
 
 Each run prints one JSON line per measurement: average milliseconds per call,
@@ -89,6 +90,20 @@ def bench_compose(op: str, rows: int, cols: int, iters: int, warmup: int, dtype=
         dg = torch.empty(cols, dtype=dtype, device=dev)
         ms = _time(lambda: _native.compose_bwd(a, b, mag, 1.0, dl, db, dg), iters, warmup)
         nbytes = 4 * e * rows * cols + 2 * e * cols
+    elif op == "linear_output_fwd":
+        # y = result + ((g - 1) * (result - bias) + g * (s * lora)) and inner = s * lora + (result - bias)
+        bias = torch.randn(cols, device=dev, generator=g).to(dtype)
+        y = torch.empty_like(a)
+        inner = torch.empty_like(a)
+        ms = _time(lambda: _native.linear_output_fwd(a, b, bias, mag, 1.0, y, inner), iters, warmup)
+        nbytes = 4 * e * rows * cols + 2 * e * cols
+    elif op == "linear_output_bwd":
+        # d_lora = g * s * dy, d_result = g * dy, d_g = column sums of inner * dy
+        dl = torch.empty_like(a)
+        dr = torch.empty_like(a)
+        dg = torch.empty(cols, dtype=dtype, device=dev)
+        ms = _time(lambda: _native.linear_output_bwd(a, b, mag, 1.0, dl, dr, dg), iters, warmup)
+        nbytes = 4 * e * rows * cols + 2 * e * cols
     else:
         raise ValueError(op)
     pk = _peaks()
@@ -100,7 +115,8 @@ def bench_compose(op: str, rows: int, cols: int, iters: int, warmup: int, dtype=
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", required=True,
-                    choices=["norm", "compose_fwd", "compose_fwd_inference", "compose_bwd", "sweep"])
+                    choices=["norm", "compose_fwd", "compose_fwd_inference", "compose_bwd", "linear_output_fwd",
+                             "linear_output_bwd", "sweep"])
     ap.add_argument("--out", type=int, default=28672)
     ap.add_argument("--in", dest="inp", type=int, default=8192)
     ap.add_argument("--rank", type=int, default=384)
