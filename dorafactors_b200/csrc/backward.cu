@@ -115,14 +115,25 @@ compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, c
     __syncthreads();
     if (is_last) {
       __threadfence();
-      if (ty == 0 && active) {
+      // All threads of the last CTA fold the tile's columns, consecutive threads on
+      // consecutive columns (coalesced partial reads), loads issued eight row-blocks
+      // at a time; the additions keep blockIdx.y order.
+      const int lin = ty * TX + tx, nthr = TX * TY;
+      const int64_t c0 = int64_t(blockIdx.x) * TX * VEC;
+      for (int j = lin; j < TX * VEC; j += nthr) {
+        const int64_t c = c0 + j;
+        if (c >= cols) break;
+        float t = 0.f;
+        unsigned y = 0;
+        for (; y + 8 <= gridDim.y; y += 8) {
+          float v[8];
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-          const int64_t c = vc * VEC + k;
-          float t = 0.f;
-          for (unsigned y = 0; y < gridDim.y; ++y) t += __ldcg(partials + int64_t(y) * cols + c);
-          d_g[c] = from_f32<TG>(t);
+          for (int q = 0; q < 8; ++q) v[q] = __ldcg(partials + int64_t(y + q) * cols + c);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) t += v[q];
         }
+        for (; y < gridDim.y; ++y) t += __ldcg(partials + int64_t(y) * cols + c);
+        d_g[c] = from_f32<TG>(t);
       }
       if (tx == 0 && ty == 0) counters[blockIdx.x] = 0u;  // ready for the next call
     }

@@ -78,9 +78,9 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     const TcGemmShape g = tc_gemm_shape(r, r, in);
     const int64_t tiles = int64_t(g.m_tiles) * g.n_tiles;
     int s = int(sms / (tiles > 0 ? tiles : 1));
-    // At least 4 (one output tile) or 8 k-blocks per split: each split's partial tile is
-    // re-read by the reduce, and a split shorter than the pipeline depth only adds latency.
-    const int per = tiles == 1 ? 4 : 8;
+    // At least 4 k-blocks per split: each split's partial tile is re-read by the reduce,
+    // and a split much shorter than the pipeline depth only adds latency.
+    const int per = 4;
     const int cap = g.kblocks / per > 0 ? g.kblocks / per : 1;
     p.gram_splits = s < 1 ? 1 : (s > cap ? cap : s);
   } else {

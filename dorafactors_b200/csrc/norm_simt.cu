@@ -122,19 +122,46 @@ __global__ void row_sumsq_kernel(const TX* __restrict__ X, int64_t M, int64_t K,
 // Gram reduction: G = sum_z Gpart[z]; writes Y = G^T in fp32 (for the
 // CUDA-core B G product) and, when hi/lo are given, the two-term split
 // Y = hi + lo with hi, lo in the half type TH (for the tensor-core product).
+// 32 x 32 tiles: the split partials are read along their rows (coalesced), summed
+// in split order, and written transposed through shared memory.
 template <typename TH>
 __global__ void gram_reduce_kernel(const float* __restrict__ part, int nsplit, int64_t r, float* __restrict__ yt,
                                    TH* __restrict__ hi, TH* __restrict__ lo) {
-  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= r * r) return;
-  const int64_t i = idx / r, j = idx % r;  // output Y[i][j] = G[j][i]
-  float v = 0.f;
-  for (int z = 0; z < nsplit; ++z) v += part[int64_t(z) * r * r + j * r + i];
-  yt[idx] = v;
-  if (hi) {
-    const TH h = from_f32<TH>(v);
-    hi[idx] = h;
-    lo[idx] = from_f32<TH>(v - to_f32(h));
+  __shared__ float tile[32][33];
+  const int64_t bi = int64_t(blockIdx.y) * 32, bj = int64_t(blockIdx.x) * 32;
+  const int tx = threadIdx.x;
+  for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
+    const int64_t i = bi + yy, j = bj + tx;  // G[i][j]
+    float v = 0.f;
+    if (i < r && j < r) {
+      // Eight split partials in flight per thread; the additions keep split order.
+      const float* p = part + i * r + j;
+      const int64_t rr = r * r;
+      int z = 0;
+      for (; z + 8 <= nsplit; z += 8) {
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = p[int64_t(z + q) * rr];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v += t[q];
+      }
+      for (; z < nsplit; ++z) v += p[int64_t(z) * rr];
+    }
+    tile[yy][tx] = v;
+  }
+  __syncthreads();
+  for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
+    const int64_t oi = bj + yy, oj = bi + tx;  // Y[oi][oj] = G[oj][oi]
+    if (oi < r && oj < r) {
+      const float v = tile[tx][yy];
+      const int64_t idx = oi * r + oj;
+      yt[idx] = v;
+      if (hi) {
+        const TH h = from_f32<TH>(v);
+        hi[idx] = h;
+        lo[idx] = from_f32<TH>(v - to_f32(h));
+      }
+    }
   }
 }
 
@@ -277,12 +304,13 @@ void launch_row_sumsq(int dx, const void* X, int64_t M, int64_t K, float* out, c
 
 void launch_gram_reduce(const float* part, int nsplit, int64_t r, float* yt, int half_dtype, void* hi, void* lo,
                         cudaStream_t st) {
-  const unsigned grid = unsigned((r * r + 255) / 256);
+  const unsigned nb = unsigned((r + 31) / 32);
+  const dim3 grid(nb, nb), block(32, 32);
   if (half_dtype == DORA_DTYPE_F16)
-    gram_reduce_kernel<__half><<<grid, 256, 0, st>>>(part, nsplit, r, yt, static_cast<__half*>(hi), static_cast<__half*>(lo));
+    gram_reduce_kernel<__half><<<grid, block, 0, st>>>(part, nsplit, r, yt, static_cast<__half*>(hi), static_cast<__half*>(lo));
   else
-    gram_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(part, nsplit, r, yt, static_cast<__nv_bfloat16*>(hi),
-                                                            static_cast<__nv_bfloat16*>(lo));
+    gram_reduce_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(part, nsplit, r, yt, static_cast<__nv_bfloat16*>(hi),
+                                                              static_cast<__nv_bfloat16*>(lo));
 }
 
 void launch_norm_finalize(const float* wpart, int nw, const float* cpart, int nc, const float* bpart, int nb,
