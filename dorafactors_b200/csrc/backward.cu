@@ -19,8 +19,9 @@ namespace dora {
 
 // kRG selects the layer-output form: the second gradient is d_result = g * d_y
 // (the base branch of y = result + delta) instead of d_base = (g - 1) * d_out.
+// At most 80 registers (three 256-thread CTAs per SM): more loads in flight per SM.
 template <typename TA, typename TG, int VEC, bool kDL, bool kDB, bool kDG, bool kRG>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
 compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, const TG* __restrict__ g, float s,
                    TA* __restrict__ d_lora, TA* __restrict__ d_base, TG* __restrict__ d_g,
                    unsigned* __restrict__ counters, float* __restrict__ partials, int64_t rows, int64_t vcols) {
