@@ -120,6 +120,30 @@ inline int check_launch(int launches = 1) {
   return e == cudaSuccess ? DORA_OK : set_cuda_error(e);
 }
 
+// Programmatic dependent launch.  A kernel started with launch_pdl may begin while
+// the previous kernel in the stream is still running (its prologue overlaps that
+// kernel's tail); it calls pdl_wait() before touching anything the previous
+// kernel writes.  pdl_trigger() lets the next such kernel start early.  Both are
+// no-ops in a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // SM count of the current device, looked up once per device.
 inline int num_sms() {
   static int cache[64] = {};

@@ -21,7 +21,7 @@
 namespace dora {
 
 struct NormPlan {
-  bool tc_u, tc_v, tc_g, fuse_v, pair_u, sk_u;
+  bool tc_u, tc_v, tc_g, fuse_v, pair_u, sk_u, sk2_u;
   SkPlan sk;
   int gram_splits, u_splits, u_ntiles, v_splits, v_ntiles;
   size_t off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, total;
@@ -57,6 +57,19 @@ static bool use_pair_kernel() {
   return on;
 }
 
+// The CTA-pair stream-K cross-term kernel runs for N tiles of 256 columns and more
+// (r > 240), where halving the A-operand bytes per SM pays for the pair's longer
+// slot hand-off (28672 x 8192: 0.205 vs 0.212 ms at r = 384; 8192 x 8192: 0.116 vs
+// 0.134 ms at r = 512, 0.066 vs 0.058 ms at r = 16).  DORA_B200_SK2=1 / 0 forces it
+// on / off.
+static int sk2_mode() {
+  static const int mode = [] {
+    const char* e = std::getenv("DORA_B200_SK2");
+    return e ? (e[0] == '1' ? 1 : 0) : -1;
+  }();
+  return mode;
+}
+
 // DORA_B200_SK=0 selects the split-K cross-term kernel instead of the stream-K one.
 static bool use_sk_kernel() {
   static const bool on = [] {
@@ -90,8 +103,8 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     if (s > kb) s = kb;
     p.gram_splits = int(s < 1 ? 1 : s);
   }
-  // Cross term: CTA pairs when the shape allows (half the per-SM operand traffic),
-  // single CTAs otherwise.
+  // Cross term: stream-K on CTA pairs (wide N tiles) or single CTAs; the split-K
+  // kernels when neither applies (or when selected for comparison).
   p.fuse_v = p.tc_u && p.tc_v && tc_can_fuse_v(out, r, in);
   if (p.tc_u) {
     const TcGemmShape u = tc_gemm_shape(out, r, in);
@@ -109,9 +122,14 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
       probe.v_part = reinterpret_cast<float*>(uintptr_t(256));
     }
     p.pair_u = use_pair_kernel() && tc2_supported(probe);
-    p.sk_u = !p.pair_u && use_sk_kernel() && tc_sk_supported(probe);
+    const int m2 = sk2_mode();
+    p.sk2_u = !p.pair_u && use_sk_kernel() && (m2 == 1 || (m2 < 0 && u.nt >= 256)) && tc2_sk_supported(probe);
+    p.sk_u = !p.pair_u && !p.sk2_u && use_sk_kernel() && tc_sk_supported(probe);
     p.u_ntiles = u.n_tiles;
-    if (p.sk_u) {
+    if (p.sk2_u) {
+      p.sk = tc2_sk_plan(out, r, in, p.fuse_v, sms);
+      p.u_splits = p.sk.slots;
+    } else if (p.sk_u) {
       p.sk = tc_sk_plan(out, r, in, p.fuse_v, sms);
       p.u_splits = p.sk.slots;
     } else {
@@ -227,6 +245,8 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
     }
     if (p.pair_u && tc2_supported(u)) rc = tc2_rowdot_gemm(u, st);
     else if (p.pair_u) return DORA_ERR_INVALID_ARGUMENT;  // planned for pairs, but B is misaligned
+    else if (p.sk2_u && tc2_sk_supported(u)) rc = tc2_sk_rowdot_gemm(u, p.sk, st);
+    else if (p.sk2_u) return DORA_ERR_INVALID_ARGUMENT;
     else if (p.sk_u && tc_sk_supported(u)) rc = tc_sk_rowdot_gemm(u, p.sk, st);
     else if (p.sk_u) return DORA_ERR_INVALID_ARGUMENT;
     else rc = tc_rowdot_gemm(u, st);

@@ -128,6 +128,8 @@ template <typename TH>
 __global__ void gram_reduce_kernel(const float* __restrict__ part, int nsplit, int64_t r, float* __restrict__ yt,
                                    TH* __restrict__ hi, TH* __restrict__ lo) {
   __shared__ float tile[32][33];
+  pdl_trigger();
+  pdl_wait();  // the Gram partials come from the previous kernel
   const int64_t bi = int64_t(blockIdx.y) * 32, bj = int64_t(blockIdx.x) * 32;
   const int tx = threadIdx.x;
   for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
@@ -181,6 +183,7 @@ __global__ void norm_finalize_kernel(const float* __restrict__ wpart, int nw, co
                                      int nc, const float* __restrict__ bpart, int nb, int64_t M, float two_s,
                                      float s2, bool scale_zero, TO* __restrict__ norm_out,
                                      float* __restrict__ parts) {
+  pdl_wait();  // the partials come from the previous kernel
   const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (m >= M) return;
   float w = 0.f, c = 0.f, b = 0.f;
@@ -306,32 +309,37 @@ void launch_gram_reduce(const float* part, int nsplit, int64_t r, float* yt, int
                         cudaStream_t st) {
   const unsigned nb = unsigned((r + 31) / 32);
   const dim3 grid(nb, nb), block(32, 32);
+  cudaError_t e;
   if (half_dtype == DORA_DTYPE_F16)
-    gram_reduce_kernel<__half><<<grid, block, 0, st>>>(part, nsplit, r, yt, static_cast<__half*>(hi), static_cast<__half*>(lo));
+    e = launch_pdl(gram_reduce_kernel<__half>, grid, block, 0, st, part, nsplit, r, yt, static_cast<__half*>(hi),
+                   static_cast<__half*>(lo));
   else
-    gram_reduce_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(part, nsplit, r, yt, static_cast<__nv_bfloat16*>(hi),
-                                                              static_cast<__nv_bfloat16*>(lo));
+    e = launch_pdl(gram_reduce_kernel<__nv_bfloat16>, grid, block, 0, st, part, nsplit, r, yt,
+                   static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
+  if (e != cudaSuccess) set_cuda_error(e);
 }
 
 void launch_norm_finalize(const float* wpart, int nw, const float* cpart, int nc, const float* bpart, int nb,
                           int64_t M, double scale, int out_dtype, void* norm_out, float* parts, cudaStream_t st) {
   const float two_s = float(2.0 * scale), s2 = float(scale * scale);
   const bool sz = (scale == 0.0);
-  const unsigned grid = unsigned((M + 255) / 256);
+  const dim3 grid(unsigned((M + 255) / 256)), block(256);
+  cudaError_t e;
   switch (out_dtype) {
     case DORA_DTYPE_BF16:
-      norm_finalize_kernel<<<grid, 256, 0, st>>>(wpart, nw, cpart, nc, bpart, nb, M, two_s, s2, sz,
-                                                 static_cast<__nv_bfloat16*>(norm_out), parts);
+      e = launch_pdl(norm_finalize_kernel<__nv_bfloat16>, grid, block, 0, st, wpart, nw, cpart, nc, bpart, nb, M,
+                     two_s, s2, sz, static_cast<__nv_bfloat16*>(norm_out), parts);
       break;
     case DORA_DTYPE_F16:
-      norm_finalize_kernel<<<grid, 256, 0, st>>>(wpart, nw, cpart, nc, bpart, nb, M, two_s, s2, sz,
-                                                 static_cast<__half*>(norm_out), parts);
+      e = launch_pdl(norm_finalize_kernel<__half>, grid, block, 0, st, wpart, nw, cpart, nc, bpart, nb, M, two_s,
+                     s2, sz, static_cast<__half*>(norm_out), parts);
       break;
     default:
-      norm_finalize_kernel<<<grid, 256, 0, st>>>(wpart, nw, cpart, nc, bpart, nb, M, two_s, s2, sz,
-                                                 static_cast<float*>(norm_out), parts);
+      e = launch_pdl(norm_finalize_kernel<float>, grid, block, 0, st, wpart, nw, cpart, nc, bpart, nb, M, two_s,
+                     s2, sz, static_cast<float*>(norm_out), parts);
       break;
   }
+  if (e != cudaSuccess) set_cuda_error(e);
 }
 
 }  // namespace dora

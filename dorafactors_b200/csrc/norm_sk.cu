@@ -152,6 +152,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
 
   const int64_t u_first = sk_begin(c, TOT, G), u_last = sk_begin(c + 1, TOT, G);
   // Segment `seg` of this CTA: tile, tile-local unit range [ua, ub), its X Y^T
@@ -219,6 +220,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         for (int j = 0; j < nzb; ++j) tma_load_2d(zbase + size_t(j) * kXTileBytes, &tmZ, zfull, j * BK, m0);
         z_seg = seg;
         for (int i = 0; i < sg.v_iters; ++i) {
+          if (gv == 0) pdl_wait();  // G (hi / lo) is written by the previous kernel
           const int64_t g = gv;
           const int vs = int(g & 1);
           if (g >= 2 && !mbar_wait(&vempty[vs], uint32_t((g / 2 - 1) & 1))) { *aborted = 1; break; }
@@ -450,7 +452,10 @@ static int launch_sk(const tc::SkArgs& k, const CUtensorMap* m, cudaStream_t st)
     if (e != cudaSuccess) return set_cuda_error(e);
     opted.fetch_or(bit, std::memory_order_relaxed);
   }
-  kfn<<<unsigned(k.grid), tc::kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], k);
+  // Launched as a programmatic dependent of the Gram reduce: the X Y^T units start at
+  // once, the producer waits for the reduce only before its first G load.
+  e = launch_pdl(kfn, dim3(unsigned(k.grid)), dim3(tc::kThreads), smem, st, m[0], m[1], m[2], m[3], m[4], k);
+  if (e != cudaSuccess) return set_cuda_error(e);
   return check_launch();
 }
 

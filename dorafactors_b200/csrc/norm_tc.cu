@@ -125,6 +125,7 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();  // the kernel after this one (Gram reduce) may be launched
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer

@@ -277,6 +277,18 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Tile row (= column of A, G and Z) held in accumulator column c when each CTA of
+// the pair stages one contiguous half of the tile's B-operand rows: chunk 0
+// (N0 = min(nt, 256) columns) takes rows [0, N0/2) from CTA 0 and [nt/2, nt/2 +
+// N0/2) from CTA 1; chunk 1 (nt - N0 columns) takes the next rows of each half.
+// The identity for nt <= 256; a swap of 64-column-aligned blocks for nt = 384, 512.
+__host__ __device__ inline int pair_col_row(int c, int nt) {
+  const int n0 = nt < 256 ? nt : 256, h0 = n0 / 2, half = nt / 2;
+  if (c < n0) return c < h0 ? c : half + (c - h0);
+  const int i = c - n0, h1 = (nt - n0) / 2;
+  return i < h1 ? h0 + i : half + h0 + (i - h1);
+}
+
 // ---------------------------------------------------------------------------
 // One 64-deep k-block of MMAs into an NT-column accumulator (NT <= 512): at most
 // two column chunks (N <= 256 each), instruction descriptors computed once.

@@ -194,11 +194,14 @@ json.dump(out, sys.stdout)
 """
 
 
-@pytest.mark.parametrize("env", [{"DORA_B200_SK": "0"}, {"DORA_B200_PAIR": "1"}], ids=["split_k", "cta_pair"])
+@pytest.mark.parametrize("env", [{"DORA_B200_SK": "0"}, {"DORA_B200_PAIR": "1"}, {"DORA_B200_SK2": "1"},
+                                 {"DORA_B200_SK2": "0"}],
+                         ids=["split_k", "cta_pair", "cta_pair_stream_k", "single_stream_k"])
 def test_cross_term_kernels_agree(env):
-    """The three tcgen05 cross-term kernels give the same fp32 terms: the default stream-K
-    kernel against the split-K kernel (DORA_B200_SK=0) and the CTA-pair kernel
-    (DORA_B200_PAIR=1), each selected in a child process."""
+    """The tcgen05 cross-term kernels give the same fp32 terms: the default choice
+    (CTA-pair stream-K for r > 240, single-CTA stream-K below) against the split-K
+    kernel (DORA_B200_SK=0), the CTA-pair split-K kernel (DORA_B200_PAIR=1) and each
+    stream-K kernel forced everywhere (DORA_B200_SK2=1 / 0), in child processes."""
     import json
     import os
     import subprocess
@@ -207,7 +210,7 @@ def test_cross_term_kernels_agree(env):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     runs = {}
     for name, extra in (("default", {}), ("other", env)):
-        e = {k: v for k, v in os.environ.items() if k not in ("DORA_B200_SK", "DORA_B200_PAIR")}
+        e = {k: v for k, v in os.environ.items() if k not in ("DORA_B200_SK", "DORA_B200_PAIR", "DORA_B200_SK2")}
         e.update(extra)
         res = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, root], env=e, capture_output=True, text=True,
                              timeout=300)
