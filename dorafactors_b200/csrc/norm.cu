@@ -88,8 +88,9 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
   p.tc_v = p.tc_u && wdt == DORA_DTYPE_BF16 && r % 8 == 0;
   // Gram partials
   if (p.tc_g) {
-    const TcGemmShape g = tc_gemm_shape(r, r, in);
-    const int64_t tiles = int64_t(g.m_tiles) * g.n_tiles;
+    // Symmetric: 128 x 128 tiles, upper triangle only.
+    const TcGemmShape g = tc_gemm_shape(r, r, in, kGramTile);
+    const int64_t tiles = int64_t(g.m_tiles) * (g.m_tiles + 1) / 2;
     int s = int(sms / (tiles > 0 ? tiles : 1));
     // At least 4 k-blocks per split: each split's partial tile is re-read by the reduce,
     // and a split much shorter than the pipeline depth only adds latency.
@@ -223,7 +224,7 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
     TcGemmArgs g{};
     g.dtype = a_dtype; g.X = A; g.Y1 = A; g.Y2 = nullptr; g.Z = nullptr; g.ldz = 0;
     g.M = R; g.N = R; g.K = K; g.mode = kGemmStore; g.sumsq = false; g.k_splits = p.gram_splits;
-    g.C = gpart;
+    g.C = gpart; g.tri = true;
     if ((rc = tc_rowdot_gemm(g, st))) return rc;
   } else {
     simt_gemm<kGemmStore, false>(a_dtype, a_dtype, a_dtype, A, K, A, K, nullptr, 0, R, R, K, p.gram_splits,
@@ -231,7 +232,7 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
     if ((rc = check_launch())) return rc;
   }
   launch_gram_reduce(gpart, p.gram_splits, R, yt, p.tc_v ? b_dtype : DORA_DTYPE_BF16, p.tc_v ? hi : nullptr,
-                     p.tc_v ? lo : nullptr, st);
+                     p.tc_v ? lo : nullptr, p.tc_g ? kGramTile : 0, st);
   if ((rc = check_launch())) return rc;
 
   // 3. cross term + ||W0||^2.

@@ -13,8 +13,10 @@ void simt_gemm(int dx, int dy, int dz, const void* X, int64_t ldx, const void* Y
                int64_t ldz, int64_t M, int64_t N, int64_t K, int ksplit, float* rowdot, float* sumsq, float* C,
                int64_t ldc, cudaStream_t st);
 void launch_row_sumsq(int dx, const void* X, int64_t M, int64_t K, float* out, cudaStream_t st);
+// tri_tile > 0: the partials hold only the tiles (i <= j) of tri_tile x tri_tile
+// blocks; the lower blocks are read from their mirror images (G is symmetric).
 void launch_gram_reduce(const float* part, int nsplit, int64_t r, float* yt, int half_dtype, void* hi, void* lo,
-                        cudaStream_t st);
+                        int tri_tile, cudaStream_t st);
 void launch_norm_finalize(const float* wpart, int nw, const float* cpart, int nc, const float* bpart, int nb,
                           int64_t M, double scale, int out_dtype, void* norm_out, float* parts, cudaStream_t st);
 
@@ -39,14 +41,18 @@ struct TcGemmArgs {
   const void* G1 = nullptr;
   const void* G2 = nullptr;
   float* v_part = nullptr;
+  // Store mode, M == N, symmetric product (the Gram matrix): 128 x 128 tiles and only
+  // those with n_tile >= m_tile are computed; C's other tiles are left unwritten.
+  bool tri = false;
 };
+constexpr int kGramTile = 128;
 struct TcGemmShape {
   int nt;        // N tile (columns of TMEM used)
   int n_tiles;
   int m_tiles;
   int kblocks;   // 64-wide k-blocks per Y operand
 };
-TcGemmShape tc_gemm_shape(int64_t M, int64_t N, int64_t K);
+TcGemmShape tc_gemm_shape(int64_t M, int64_t N, int64_t K, int force_nt = 0);
 bool tc_gemm_supported(int dtype, int64_t M, int64_t N, int64_t K, const void* X, const void* Y, const void* Z,
                        int64_t ldz);
 int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st);

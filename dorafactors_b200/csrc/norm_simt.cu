@@ -126,14 +126,18 @@ __global__ void row_sumsq_kernel(const TX* __restrict__ X, int64_t M, int64_t K,
 // in split order, and written transposed through shared memory.
 template <typename TH>
 __global__ void gram_reduce_kernel(const float* __restrict__ part, int nsplit, int64_t r, float* __restrict__ yt,
-                                   TH* __restrict__ hi, TH* __restrict__ lo) {
+                                   TH* __restrict__ hi, TH* __restrict__ lo, int tri_tile) {
   __shared__ float tile[32][33];
   pdl_trigger();
   pdl_wait();  // the Gram partials come from the previous kernel
   const int64_t bi = int64_t(blockIdx.y) * 32, bj = int64_t(blockIdx.x) * 32;
+  // A block below the computed triangle is read from its mirror (bj, bi), which
+  // then needs no transpose on the way out.
+  const bool mirror = tri_tile > 0 && (bi / tri_tile) > (bj / tri_tile);
+  const int64_t ri = mirror ? bj : bi, rj = mirror ? bi : bj;
   const int tx = threadIdx.x;
   for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
-    const int64_t i = bi + yy, j = bj + tx;  // G[i][j]
+    const int64_t i = ri + yy, j = rj + tx;  // partial element [i][j]
     float v = 0.f;
     if (i < r && j < r) {
       // Eight split partials in flight per thread; the additions keep split order.
@@ -155,7 +159,7 @@ __global__ void gram_reduce_kernel(const float* __restrict__ part, int nsplit, i
   for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
     const int64_t oi = bj + yy, oj = bi + tx;  // Y[oi][oj] = G[oj][oi]
     if (oi < r && oj < r) {
-      const float v = tile[tx][yy];
+      const float v = mirror ? tile[yy][tx] : tile[tx][yy];
       const int64_t idx = oi * r + oj;
       yt[idx] = v;
       if (hi) {
@@ -306,16 +310,16 @@ void launch_row_sumsq(int dx, const void* X, int64_t M, int64_t K, float* out, c
 }
 
 void launch_gram_reduce(const float* part, int nsplit, int64_t r, float* yt, int half_dtype, void* hi, void* lo,
-                        cudaStream_t st) {
+                        int tri_tile, cudaStream_t st) {
   const unsigned nb = unsigned((r + 31) / 32);
   const dim3 grid(nb, nb), block(32, 32);
   cudaError_t e;
   if (half_dtype == DORA_DTYPE_F16)
     e = launch_pdl(gram_reduce_kernel<__half>, grid, block, 0, st, part, nsplit, r, yt, static_cast<__half*>(hi),
-                   static_cast<__half*>(lo));
+                   static_cast<__half*>(lo), tri_tile);
   else
     e = launch_pdl(gram_reduce_kernel<__nv_bfloat16>, grid, block, 0, st, part, nsplit, r, yt,
-                   static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
+                   static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), tri_tile);
   if (e != cudaSuccess) set_cuda_error(e);
 }
 

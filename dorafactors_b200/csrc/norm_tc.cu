@@ -55,6 +55,7 @@ struct KArgs {
   float* sumsq_part;     // [k_splits][M]
   float* v_part;         // fused B G B^T partials, [k_splits][M]
   float* C;              // store mode: [k_splits][M][N]
+  int tri;               // store mode: only tiles with n_tile >= m_tile (a symmetric product)
 };
 
 template <typename T, int MODE, bool kSumSq>
@@ -81,10 +82,25 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int unit = blockIdx.x;
-  const int m_tile = unit % a.m_tiles;
-  const int rest = unit / a.m_tiles;
-  const int n_tile = rest % a.n_tiles;
-  const int ks = rest / a.n_tiles;
+  int m_tile, n_tile, ks;
+  if (a.tri) {
+    // Upper-triangular tile pairs (i <= j) of a symmetric product, then the K split.
+    const int per = a.m_tiles * (a.m_tiles + 1) / 2;
+    int t = unit % per;
+    ks = unit / per;
+    int i = 0;
+    while (t >= a.m_tiles - i) {
+      t -= a.m_tiles - i;
+      ++i;
+    }
+    m_tile = i;
+    n_tile = i + t;
+  } else {
+    m_tile = unit % a.m_tiles;
+    const int rest = unit / a.m_tiles;
+    n_tile = rest % a.n_tiles;
+    ks = rest / a.n_tiles;
+  }
   const int64_t m0 = int64_t(m_tile) * BM;
   const int64_t n0 = int64_t(n_tile) * nt;
   const int kb_total = a.two_y ? 2 * a.kblocks : a.kblocks;
@@ -351,9 +367,12 @@ static int stages_for(int nt) {
 
 }  // namespace tc
 
-TcGemmShape tc_gemm_shape(int64_t M, int64_t N, int64_t K) {
+TcGemmShape tc_gemm_shape(int64_t M, int64_t N, int64_t K, int force_nt) {
   TcGemmShape s;
-  if (N <= 256) {
+  if (force_nt > 0 && N > force_nt) {
+    s.nt = force_nt;
+    s.n_tiles = int((N + force_nt - 1) / force_nt);
+  } else if (N <= 256) {
     s.nt = int((N + 15) / 16 * 16);
     s.n_tiles = 1;
   } else if (N <= 512) {
@@ -419,7 +438,8 @@ bool tc_can_fuse_v(int64_t M, int64_t N, int64_t K) {
 }
 
 int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st) {
-  const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K);
+  const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K, a.tri ? kGramTile : 0);
+  if (a.tri && (a.mode != kGemmStore || a.M != a.N || sh.m_tiles != sh.n_tiles)) return DORA_ERR_INVALID_ARGUMENT;
   const int kb_total = a.Y2 ? 2 * sh.kblocks : sh.kblocks;
   if (a.k_splits < 1 || a.k_splits > kb_total) return DORA_ERR_INVALID_ARGUMENT;
   const int ybox = sh.nt <= 256 ? sh.nt : 128;
@@ -468,7 +488,9 @@ int tc_rowdot_gemm(const TcGemmArgs& a, cudaStream_t st) {
   k.sumsq_part = a.sumsq_part;
   k.v_part = a.v_part;
   k.C = a.C;
-  const unsigned grid = unsigned(sh.m_tiles) * unsigned(sh.n_tiles) * unsigned(a.k_splits);
+  k.tri = a.tri ? 1 : 0;
+  const unsigned tiles = a.tri ? unsigned(sh.m_tiles * (sh.m_tiles + 1) / 2) : unsigned(sh.m_tiles) * unsigned(sh.n_tiles);
+  const unsigned grid = tiles * unsigned(a.k_splits);
   if (a.dtype == DORA_DTYPE_BF16) return dispatch_tc<__nv_bfloat16>(a, k, grid, mx, my1, my2, mz, mg1, mg2, st);
   return dispatch_tc<__half>(a, k, grid, mx, my1, my2, mz, mg1, mg2, st);
 }
