@@ -352,9 +352,11 @@ def run_native(args) -> None:
                 kernels[name] = {**st, "algorithmic_bytes": hbm_bytes[name], "achieved_gbs": a,
                                  "frac": a / peaks["hbm_gbs"]}
             elif name == "weight_norm":
+                # Timed inside a long step: against the sustained (power-capped) GEMM peak.
                 a = norm_flops(OUT_F, IN_F, RANK) / (st["avg_ms"] * 1e-3) / 1e12
                 kernels[name] = {**st, "algorithmic_flops": norm_flops(OUT_F, IN_F, RANK), "achieved_tflops": a,
-                                 "frac": a / peaks["bf16_tflops"]}
+                                 "peak_tflops": peaks["bf16_tflops_sustained"], "peak_kind": "sustained",
+                                 "frac": a / peaks["bf16_tflops_sustained"]}
         dom = max(kern, key=lambda n: kern[n]["total_ms"]) if kern else None
         roof = None
         if dom in hbm_bytes:
@@ -363,7 +365,7 @@ def run_native(args) -> None:
                     "traffic": read_traffic(dom), "algorithmic_bytes": hbm_bytes[dom], "peak_source": peak_src}
         elif dom == "weight_norm":
             roof = {"kernel": dom, "bound": "tensor", "achieved": kernels[dom]["achieved_tflops"],
-                    "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": kernels[dom]["frac"],
+                    "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s", "frac": kernels[dom]["frac"],
                     "traffic": read_traffic(dom), "algorithmic_flops": norm_flops(OUT_F, IN_F, RANK),
                     "peak_source": peak_src}
         value = TOKENS * world / (ms * 1e-3)

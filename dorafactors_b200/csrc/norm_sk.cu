@@ -46,15 +46,15 @@ __host__ __device__ inline int64_t sk_owner(int64_t x, int64_t total, int64_t gr
 
 struct SkArgs {
   int64_t M, N;
-  int nt, ybox, m_tiles, kblocks, stages, grid, slots;
+  int nt, ybox, m_tiles, n_tiles, kblocks, stages, grid, slots;
   int apart;           // Z and the G slots have their own region after the ring (else they reuse the ring)
   uint32_t stage_off;  // Z / G region, from the 1024-aligned base
   uint32_t bar_off;    // barriers, from the 1024-aligned base
   int fuse_v, v_kblocks;
   int64_t units_per_tile, total_units;
   uint32_t tmem_cols;
-  float* rowdot_part;  // [slots][M]
-  float* sumsq_part;   // [slots][M]
+  float* rowdot_part;  // [slots * n_tiles][M], entry (slot * n_tiles + n_tile)
+  float* sumsq_part;   // [slots][M] (from the n_tile = 0 tiles)
   float* v_part;       // [slots][M] when fuse_v
 };
 
@@ -158,12 +158,16 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
   // Segment `seg` of this CTA: tile, tile-local unit range [ua, ub), its X Y^T
   // part [ua, min(ub, kbt)) and its Z G^T part [max(ua, kbt), ub) - kbt.
   struct Seg {
-    int64_t tile;
-    int ua, ub, u_iters, v0, v_iters;
+    int64_t tile, m_tile;
+    int n_tile, ua, ub, u_iters, v0, v_iters;
   };
+  // Tiles run N-tile fastest, so the N tiles of one row block stream the same W0
+  // rows close together in time (L2 reuse).
   auto segment = [&](int64_t u) {
     Seg s;
     s.tile = u / TU;
+    s.m_tile = s.tile / a.n_tiles;
+    s.n_tile = int(s.tile % a.n_tiles);
     s.ua = int(u - s.tile * TU);
     const int64_t e = u_last - s.tile * TU;
     s.ub = int(e < TU ? e : TU);
@@ -185,7 +189,8 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       for (int64_t u = u_first; u < u_last && !*aborted; ++seg) {
         const Seg sg = segment(u);
         u = sg.tile * TU + sg.ub;
-        const int m0 = int(sg.tile * BM);
+        const int m0 = int(sg.m_tile * BM);
+        const int n0 = sg.n_tile * nt;
         // Ring mode: the previous segment's epilogues must be done with the staged Z / G
         // (which live in the ring) before the ring is refilled.
         if (!a.apart && seg > 0 && !mbar_wait(seg_free, (seg - 1) & 1)) { *aborted = 1; break; }
@@ -199,11 +204,11 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
           mbar_expect_tx(&full[s], stage_bytes);
           tma_load_2d(sX, &tmX, &full[s], kx, m0);
           for (int j = 0; j * a.ybox < nt; ++j)
-            tma_load_2d(sX + kXTileBytes + size_t(j) * a.ybox * 128, &tmY, &full[s], kx, j * a.ybox);
+            tma_load_2d(sX + kXTileBytes + size_t(j) * a.ybox * 128, &tmY, &full[s], kx, n0 + j * a.ybox);
           ++gk;
           // Start the tile's Z rows towards L2 a few k-blocks before they are staged.
           if (i == (sg.u_iters > S + 1 ? sg.u_iters - S - 1 : 0))
-            for (int j = 0; j < nzb; ++j) tma_prefetch_2d(&tmZ, j * BK, m0);
+            for (int j = 0; j < nzb; ++j) tma_prefetch_2d(&tmZ, n0 + j * BK, m0);
         }
         if (*aborted) break;
         bool ok = true;
@@ -217,7 +222,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         }
         if (!ok) { *aborted = 1; break; }
         mbar_expect_tx(zfull, z_bytes);
-        for (int j = 0; j < nzb; ++j) tma_load_2d(zbase + size_t(j) * kXTileBytes, &tmZ, zfull, j * BK, m0);
+        for (int j = 0; j < nzb; ++j) tma_load_2d(zbase + size_t(j) * kXTileBytes, &tmZ, zfull, n0 + j * BK, m0);
         z_seg = seg;
         for (int i = 0; i < sg.v_iters; ++i) {
           if (gv == 0) pdl_wait();  // G (hi / lo) is written by the previous kernel
@@ -297,9 +302,10 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16);
+    int cur_n0 = 0;  // first column of the current segment's N tile
     auto rowdot_epilogue = [&]() -> float {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      const int64_t ncols = a.N;
+      const int64_t ncols = a.N - cur_n0;
       int c0 = 0;
       for (; c0 + 64 <= int(a.tmem_cols) && c0 < nt && c0 < ncols; c0 += 64) {
         float v[64];
@@ -321,14 +327,23 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
     for (int64_t u = u_first; u < u_last; ++seg) {
       const Seg sg = segment(u);
       u = sg.tile * TU + sg.ub;
-      const int64_t m = sg.tile * BM + row;
+      const int64_t m = sg.m_tile * BM + row;
+      cur_n0 = sg.n_tile * nt;
+      const bool ssq_tile = sg.n_tile == 0;  // ||X||^2 once per row block
       float ssq = 0.f;
       bool ok = true;
       if (kSumSq) {
         for (int i = 0; i < sg.u_iters; ++i) {
           const int64_t g = gk++;
           const int s = int(g % S);
+          // Every ring use is released by the row warps too (fixed barrier count); the
+          // data is summed only in the N tile that owns ||X||^2.
           if (!__all_sync(0xffffffffu, mbar_wait(&full[s], uint32_t((g / S) & 1)))) { ok = false; break; }
+          if (!ssq_tile) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            continue;
+          }
           const uint8_t* rowp = base + size_t(s) * stage_bytes + row * 128;
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
@@ -357,8 +372,8 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       tc_fence_after();
       const float cacc = sg.u_iters > 0 ? rowdot_epilogue() : 0.f;
       if (m < a.M) {
-        a.rowdot_part[int64_t(slot) * a.M + m] = cacc;
-        a.sumsq_part[int64_t(slot) * a.M + m] = ssq;
+        a.rowdot_part[(int64_t(slot) * a.n_tiles + sg.n_tile) * a.M + m] = cacc;
+        if (ssq_tile) a.sumsq_part[int64_t(slot) * a.M + m] = ssq;
       }
       float bacc = 0.f;
       if (sg.v_iters > 0) {
@@ -381,8 +396,8 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         // Zero the slots this tile does not use, so the finalize sums a fixed count.
         const int used = int(sk_owner(sg.tile * TU + TU - 1, TOT, G) - first) + 1;
         for (int s2 = used; s2 < a.slots; ++s2) {
-          a.rowdot_part[int64_t(s2) * a.M + m] = 0.f;
-          a.sumsq_part[int64_t(s2) * a.M + m] = 0.f;
+          a.rowdot_part[(int64_t(s2) * a.n_tiles + sg.n_tile) * a.M + m] = 0.f;
+          if (ssq_tile) a.sumsq_part[int64_t(s2) * a.M + m] = 0.f;
           if (a.fuse_v) a.v_part[int64_t(s2) * a.M + m] = 0.f;
         }
       }
@@ -409,7 +424,7 @@ bool tc_sk_supported(const TcGemmArgs& a) {
       !aligned16(a.Z))
     return false;
   const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K);
-  if (sh.n_tiles != 1) return false;
+  if (sh.n_tiles != 1 && a.G1) return false;  // the fused B G B^T phase needs the whole row in one tile
   const tc::SkLayout L = tc::sk_layout(sh.nt, a.G1 != nullptr);
   const uint32_t z_bytes = uint32_t((sh.nt + tc::BK - 1) / tc::BK) * tc::kXTileBytes;
   const uint32_t staging = z_bytes + (a.G1 ? 2u * uint32_t(sh.nt) * 128u : 0u);
@@ -422,14 +437,15 @@ SkPlan tc_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
   const TcGemmShape sh = tc_gemm_shape(M, N, K);
   SkPlan p;
   p.units_per_tile = int64_t(sh.kblocks) + (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
-  p.total_units = int64_t(sh.m_tiles) * p.units_per_tile;
+  const int64_t tiles = int64_t(sh.m_tiles) * sh.n_tiles;
+  p.total_units = tiles * p.units_per_tile;
   // One CTA per SM, but no CTA with fewer than four units (each segment pays a staging and epilogue).
   int64_t g = p.total_units / 4;
   if (g > sms) g = sms;
   if (g < 1) g = 1;
   p.grid = int(g);
   int slots = 1;
-  for (int64_t t = 0; t < sh.m_tiles; ++t) {
+  for (int64_t t = 0; t < tiles; ++t) {
     const int64_t f = tc::sk_owner(t * p.units_per_tile, p.total_units, g);
     const int64_t l = tc::sk_owner(t * p.units_per_tile + p.units_per_tile - 1, p.total_units, g);
     if (int(l - f + 1) > slots) slots = int(l - f + 1);
@@ -479,6 +495,7 @@ int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.nt = sh.nt;
   k.ybox = ybox;
   k.m_tiles = sh.m_tiles;
+  k.n_tiles = sh.n_tiles;
   k.kblocks = sh.kblocks;
   const tc::SkLayout L = tc::sk_layout(sh.nt, fuse);
   k.stages = L.stages;
@@ -490,7 +507,7 @@ int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.fuse_v = fuse ? 1 : 0;
   k.v_kblocks = int((a.N + tc::BK - 1) / tc::BK);
   k.units_per_tile = int64_t(sh.kblocks) + (fuse ? 2 * k.v_kblocks : 0);
-  k.total_units = int64_t(sh.m_tiles) * k.units_per_tile;
+  k.total_units = int64_t(sh.m_tiles) * sh.n_tiles * k.units_per_tile;
   if (k.units_per_tile != p.units_per_tile || k.total_units != p.total_units) return DORA_ERR_INVALID_ARGUMENT;
   uint32_t cols = 32;
   while (cols < uint32_t(sh.nt)) cols <<= 1;
