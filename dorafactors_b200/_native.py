@@ -39,6 +39,10 @@ SIGNATURES = {
     "dora_compose_fwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _int, _vp]),
     "dora_compose_bwd_workspace_size": (_sz, [_i64, _i64, _int]),
     "dora_compose_bwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
+    "dora_compose_fwd_channels": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "dora_compose_bwd_channels_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
+    "dora_compose_bwd_channels": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _i64,
+                                         _int, _vp]),
     "dora_linear_output_fwd": (_int, [_vp, _vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _int, _vp]),
     "dora_linear_output_bwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
     "dora_compose_bwd_noalloc": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
@@ -153,10 +157,16 @@ _ws_lock = threading.Lock()
 
 
 def bwd_workspace(device: torch.device, rows: int, cols: int, act_code: int) -> tuple[torch.Tensor | None, int]:
-    need = load_library().dora_compose_bwd_workspace_size(rows, cols, act_code)
+    return _zeroed_workspace(device, load_library().dora_compose_bwd_workspace_size(rows, cols, act_code), "linear")
+
+
+def _zeroed_workspace(device: torch.device, need: int, kind: str) -> tuple[torch.Tensor | None, int]:
+    """A backward workspace per (device, stream, kind): completion counters that the
+    kernels leave at zero, then scratch partials.  The linear and the channel-layout
+    backward lay these out differently, so each kind keeps its own buffer."""
     if need == 0:
         return None, 0
-    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream, kind)
     with _ws_lock:
         buf = _ws_cache.get(key)
         if buf is None or buf.numel() < need:
@@ -196,6 +206,32 @@ def compose_bwd(d_out2d, inner2d, g1d, scale: float, d_lora2d, d_base2d, d_g1d) 
         ptr(d_g1d), ptr(ws), nbytes, rows, cols, act, stream_ptr(dev),
     )
     check(code, "dora_compose_bwd")
+
+
+def compose_fwd_channels(lora, base, g1d, scale: float, out, inner, batch: int, channels: int, spatial: int) -> None:
+    """Conv-layout compose: contiguous [batch, channels, spatial...] tensors, g per channel."""
+    dev = lora.device
+    code = load_library().dora_compose_fwd_channels(
+        ptr(lora), ptr(base), ptr(g1d), dtype_code(g1d), float(scale), ptr(out), ptr(inner), batch, channels,
+        spatial, dtype_code(lora), stream_ptr(dev),
+    )
+    check(code, "dora_compose_fwd_channels")
+
+
+def compose_bwd_channels(d_out, inner, g1d, scale: float, d_lora, d_base, d_g1d, batch: int, channels: int,
+                         spatial: int) -> None:
+    dev = d_out.device
+    act = dtype_code(d_out)
+    ws, nbytes = (None, 0)
+    if d_g1d is not None:
+        ws, nbytes = _zeroed_workspace(
+            dev, load_library().dora_compose_bwd_channels_workspace_size(batch, channels, spatial, act), "channels"
+        )
+    code = load_library().dora_compose_bwd_channels(
+        ptr(d_out), ptr(inner), ptr(g1d), dtype_code(g1d), float(scale), ptr(d_lora), ptr(d_base), ptr(d_g1d),
+        ptr(ws), nbytes, batch, channels, spatial, act, stream_ptr(dev),
+    )
+    check(code, "dora_compose_bwd_channels")
 
 
 def linear_output_fwd(lora2d, result2d, bias1d, g1d, scale: float, y2d, inner2d) -> None:

@@ -17,8 +17,12 @@ What changed underneath:
     O(out + r^2) floats regardless of ``in``, and the no-``base_result`` path
     forms the base output in one GEMM, which 180 GB of HBM holds for any
     practical layer.
-ZeRO-3 / FSDP parameter gathering, quantized base weights, conv and embedding
-DoRA are outside this package.
+Convolution and embedding layers (``DoraConv1d/2d/3dLayer``,
+``DoraEmbeddingLayer``, dora.py:1491-1742) reuse the native factored norm on
+flattened (conv) or transposed (embedding) weights; the embedding norm no longer
+forms the dense [num_embeddings x embedding_dim] delta the reference builds.
+ZeRO-3 / FSDP parameter gathering and quantized base weights are outside this
+package.
 """
 
 from __future__ import annotations
@@ -44,6 +48,10 @@ from .dora_fused import (
 logger = logging.getLogger(__name__)
 
 __all__ = [
+    "DoraConv1dLayer",
+    "DoraConv2dLayer",
+    "DoraConv3dLayer",
+    "DoraEmbeddingLayer",
     "DoraLinearLayer",
     "fused_dora_compose",
     "fused_dora_compose_autograd",
@@ -206,13 +214,17 @@ class DoraLinearLayer(nn.Module):
         if dtype_is_fp16:
             lora_A = lora_A.float()
             lora_B = lora_B.float()
-        weight = base_layer.weight
-        if weight.data.ndim >= 3:
-            raise NotImplementedError("convolutional DoRA layers are not implemented by dorafactors_b200")
-        weight = weight.to(lora_A.device)
-        weight_norm = self._get_weight_norm_linear(
-            base_weight=weight, lora_A_w=lora_A, lora_B_w=lora_B, scaling=scaling
-        )
+        weight = base_layer.weight.to(lora_A.device)
+        if weight.data.ndim >= 3:  # convolution weights (dora.py:1358-1364)
+            if not hasattr(self, "_get_weight_norm_conv_factored"):
+                raise NotImplementedError("a convolution weight needs a DoraConvNdLayer")
+            weight_norm = self._get_weight_norm_conv_factored(
+                base_weight=weight, lora_A_w=lora_A, lora_B_w=lora_B, scaling=scaling
+            )
+        else:
+            weight_norm = self._get_weight_norm_linear(
+                base_weight=weight, lora_A_w=lora_A, lora_B_w=lora_B, scaling=scaling
+            )
         if dtype_is_fp16:
             weight_norm = weight_norm.half()
         if place_on_cpu:
@@ -315,3 +327,176 @@ class DoraLinearLayer(nn.Module):
 
     def __repr__(self) -> str:
         return "lora.dora." + super().__repr__()
+
+
+class DoraEmbeddingLayer(DoraLinearLayer):
+    """DoRA magnitude module for an embedding (dora.py:1491-1590), built with
+    ``fan_in_fan_out=True`` by PEFT's ``DoraEmbeddingVariant`` (variants.py:287-300).
+
+    The magnitude holds one value per embedding dimension: the norm is taken over
+    the vocabulary, ``||W[:, j] + s (lora_A lora_B)[:, j]||``.  With ``W0 = W^T``,
+    ``A = lora_A^T`` and ``B = lora_B^T`` that is the factored row norm of the linear
+    layer, so it runs natively without forming the [V x d] delta.
+    """
+
+    def forward(self, x, *, lora_A, lora_B, scaling, base_layer, embed_fn, base_result=None):
+        """Return ``(mag_norm_scale, delta)``; ``lora_A`` [V x r] and ``lora_B`` [r x d] are
+        the transposed adapter tensors, as ``DoraEmbeddingVariant.forward`` passes them."""
+        magnitude = self.weight
+        with torch.no_grad(), _disable_autocast(base_layer.weight.device.type):
+            weight_norm = self._get_weight_norm_linear(
+                base_weight=base_layer.weight, lora_A_w=lora_A.T, lora_B_w=lora_B.T, scaling=scaling
+            )
+        if weight_norm.device != magnitude.device:
+            weight_norm = weight_norm.to(device=magnitude.device)
+        eps = 1e-12 if weight_norm.dtype in (torch.float32, torch.float64) else 1e-6
+        mag_norm_scale = magnitude / weight_norm.clamp_min(eps)
+        if base_result is None:
+            weight = base_layer.weight
+            if weight.device != x.device:
+                weight = weight.to(device=x.device)
+            base_result = embed_fn(x, weight)
+        lora_out = embed_fn(x, lora_A) @ lora_B
+        if base_result.dtype != lora_out.dtype:
+            base_result = base_result.to(lora_out.dtype)
+        result_dora = self._compose_with_dispatch(
+            lora_out=lora_out, base_result=base_result, mag_norm_scale=mag_norm_scale, scale=scaling
+        )
+        return mag_norm_scale, result_dora
+
+
+class _DoraConvNdLayer(DoraLinearLayer):
+    """DoRA magnitude module for Conv1d/2d/3d (dora.py:1593-1724).
+
+    The norm is the linear factored norm on the flattened weights
+    ``W [out, in/groups * k...]``, ``A [r, in/groups * k...]``, ``B [out, r]`` (grouped
+    adapters expand B block-diagonally, dora.py:1612-1624); the compose runs on the
+    native channel-layout kernels (g per output channel of [N, C, *spatial]).
+    The magnitude has shape [1, out, 1, ...].
+    """
+
+    conv_fn = None
+
+    @torch.no_grad()
+    def _get_weight_norm_conv_factored(self, *, base_weight, lora_A_w, lora_B_w, scaling, chunk_size=None):
+        out_channels = base_weight.shape[0]
+        flat_weight = base_weight.reshape(out_channels, -1)
+        rank = lora_A_w.shape[0]
+        flat_A = lora_A_w.reshape(rank, -1)
+        flat_B = lora_B_w.reshape(out_channels, -1)
+        rank_per_group = flat_B.shape[1]
+        if rank_per_group > 0 and rank % rank_per_group == 0:
+            groups = rank // rank_per_group
+            if groups > 1 and out_channels % groups == 0:
+                out_per_group = out_channels // groups
+                expanded = flat_B.new_zeros((out_channels, rank))
+                for gi in range(groups):
+                    rows = slice(gi * out_per_group, (gi + 1) * out_per_group)
+                    cols = slice(gi * rank_per_group, (gi + 1) * rank_per_group)
+                    expanded[rows, cols] = flat_B[rows, :]
+                flat_B = expanded
+        saved = self.fan_in_fan_out
+        self.fan_in_fan_out = False  # conv weights are never stored transposed
+        try:
+            norms = self._get_weight_norm_linear(
+                base_weight=flat_weight, lora_A_w=flat_A, lora_B_w=flat_B, scaling=scaling, chunk_size=chunk_size
+            )
+        finally:
+            self.fan_in_fan_out = saved
+        return norms.view((1, out_channels) + (1,) * max(0, base_weight.dim() - 2))
+
+    @torch.no_grad()
+    def get_weight_norm(self, weight, lora_weight, scaling) -> torch.Tensor:
+        """Dense ``||W + s * lora_weight||`` per output channel, shaped [1, out, 1, ...] (dora.py:1636-1646)."""
+        out_channels = weight.shape[0]
+        W = weight.reshape(out_channels, -1)
+        _native.require_cuda(W, what="get_weight_norm")
+        if W.dtype not in _native.DTYPE_CODE:
+            raise ValueError(f"Unsupported weight dtype {W.dtype} for DoRA norm computation.")
+        L = lora_weight.to(device=W.device).reshape(out_channels, -1)
+        if L.dtype not in _native.DTYPE_CODE:
+            L = L.float()
+        out = torch.empty(out_channels, dtype=W.dtype, device=W.device)
+        _native.weight_norm_dense(W.contiguous(), L.contiguous(), float(scaling), out)
+        return out.view((1, out_channels) + (1,) * max(0, weight.dim() - 2))
+
+    def _compose_with_dispatch(self, *, lora_out, base_result, mag_norm_scale, scale):
+        from .dora_fused import fused_dora_compose_channels
+
+        return fused_dora_compose_channels(lora_out, base_result, mag_norm_scale, scale)
+
+    def forward(self, x, *, lora_A, lora_B, scaling, base_layer, base_result=None):
+        """DoRA delta of a convolution (dora.py:1648-1715): norm under ``no_grad`` and
+        detached, ``g = m / clamp_min(norm, eps)``, compose on the native kernels."""
+        magnitude = self.weight
+        with torch.no_grad(), _disable_autocast(base_layer.weight.device.type):
+            weight = base_layer.weight
+            weight_norm = self._get_weight_norm_conv_factored(
+                base_weight=weight, lora_A_w=lora_A.weight, lora_B_w=lora_B.weight, scaling=scaling
+            )
+        if weight_norm.device != magnitude.device:
+            weight_norm = weight_norm.to(device=magnitude.device)
+        eps = 1e-12 if weight_norm.dtype in (torch.float32, torch.float64) else 1e-6
+        mag_norm_scale = magnitude / weight_norm.clamp_min(eps)
+        if base_result is None:
+            w = base_layer.weight
+            if w.device != x.device or w.dtype != x.dtype:
+                w = w.to(device=x.device, dtype=x.dtype)
+            base_result = self.conv_fn(
+                x, w, bias=None, stride=base_layer.stride, padding=base_layer.padding,
+                dilation=base_layer.dilation, groups=base_layer.groups,
+            )
+        else:
+            bias = base_layer.bias
+            if bias is not None:
+                if bias.device != base_result.device or bias.dtype != base_result.dtype:
+                    bias = bias.to(device=base_result.device, dtype=base_result.dtype)
+                base_result = base_result - bias.view((1, -1) + (1,) * (base_result.dim() - 2))
+        lora_out = lora_B(lora_A(x))
+        if base_result.dtype != lora_out.dtype:
+            base_result = base_result.to(lora_out.dtype)
+        return self._compose_with_dispatch(
+            lora_out=lora_out, base_result=base_result, mag_norm_scale=mag_norm_scale, scale=scaling
+        )
+
+
+class DoraConv1dLayer(_DoraConvNdLayer):
+    conv_fn = staticmethod(F.conv1d)
+
+
+class DoraConv2dLayer(_DoraConvNdLayer):
+    conv_fn = staticmethod(F.conv2d)
+
+
+class DoraConv3dLayer(_DoraConvNdLayer):
+    conv_fn = staticmethod(F.conv3d)
+
+
+# ---------------------------------------------------------------------------
+# Merge / unmerge of a linear DoRA adapter into the base weight
+# (DoraLinearVariant.merge_safe / merge_unsafe / unmerge, variants.py:164-212).
+# ---------------------------------------------------------------------------
+@torch.no_grad()
+def merge_weight(base_weight, lora_A_w, lora_B_w, magnitude, scaling, fan_in_fan_out=False):
+    """Return ``(merged_weight, weight_norm)`` with
+    ``merged = (m / ||W + s B A||) * (W + s B A)`` in the weight's dtype and layout.
+
+    The norm is the native factored norm (the reference forms it densely from the
+    delta, variants.py:168-173; same value within fp32 rounding).  Keep
+    ``weight_norm`` for ``unmerge_weight``: it must be the norm of the original
+    weight, as the reference caches it."""
+    layer = DoraLinearLayer(fan_in_fan_out=fan_in_fan_out)
+    norm = layer._get_weight_norm_linear(base_weight=base_weight, lora_A_w=lora_A_w, lora_B_w=lora_B_w,
+                                         scaling=scaling)
+    delta = _transpose((lora_B_w.float() @ lora_A_w.float()) * scaling, fan_in_fan_out)
+    factor = _transpose((magnitude.detach().float() / norm.float()).view(-1, 1), fan_in_fan_out)
+    merged = (factor * (base_weight.float() + delta)).to(base_weight.dtype)
+    return merged, norm
+
+
+@torch.no_grad()
+def unmerge_weight(merged_weight, lora_A_w, lora_B_w, magnitude, weight_norm, scaling, fan_in_fan_out=False):
+    """Invert ``merge_weight``: ``W = merged / (m / norm) - s B A`` (variants.py:202-212)."""
+    delta = _transpose((lora_B_w.float() @ lora_A_w.float()) * scaling, fan_in_fan_out)
+    factor = _transpose((magnitude.detach().float() / weight_norm.float()).view(-1, 1), fan_in_fan_out)
+    return (merged_weight.float() / factor - delta).to(merged_weight.dtype)

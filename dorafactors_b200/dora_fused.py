@@ -407,3 +407,73 @@ def fused_dora_compose_autograd(
                                                             mag_norm_scale.requires_grad)
         return out
     return FusedDoRAComposeFunction.apply(lora, base, mag_norm_scale, scale)
+
+
+# ---------------------------------------------------------------------------
+# Convolution layout: activations [batch, channels, *spatial], g per channel
+# (the compose of _DoraConvNdLayer.forward, dora.py:1670-1715; the reference
+# evaluates it eagerly, dora.py:1331-1334).
+# ---------------------------------------------------------------------------
+def _prepare_channels(lora: torch.Tensor, base: torch.Tensor, mag: torch.Tensor, what: str):
+    _native.require_cuda(lora, base, mag, what=what)
+    if lora.shape != base.shape:
+        raise ValueError(f"{what}: lora {tuple(lora.shape)} and base {tuple(base.shape)} differ in shape")
+    if lora.ndim < 2:
+        raise ValueError(f"{what}: expected [batch, channels, *spatial] activations, got {tuple(lora.shape)}")
+    channels = lora.shape[1]
+    if mag.numel() != channels or (mag.ndim >= 2 and mag.shape[1] != channels):
+        raise ValueError(f"mag_norm_scale {tuple(mag.shape)} does not hold one value per channel ({channels})")
+    batch = lora.shape[0]
+    spatial = lora.numel() // (batch * channels) if batch and channels else 0
+    if base.dtype != lora.dtype:
+        base = base.to(lora.dtype)
+    g = mag.reshape(-1)
+    if g.dtype not in (lora.dtype, torch.float32):
+        g = g.float()
+    return lora.contiguous(), base.contiguous(), g.contiguous(), batch, channels, spatial
+
+
+class FusedDoRAComposeChannelsFunction(torch.autograd.Function):
+    """Conv-layout compose with the native fused backward; saves ``inner`` only when
+    the magnitude needs a gradient, like ``FusedDoRAComposeFunction``."""
+
+    @staticmethod
+    def forward(ctx, lora, base, mag_norm_scale, scale):
+        l, b, g, n, c, sp = _prepare_channels(lora, base, mag_norm_scale, "fused_dora_compose_channels")
+        out = torch.empty_like(l)
+        inner = torch.empty_like(l) if mag_norm_scale.requires_grad else None
+        if out.numel():
+            _native.compose_fwd_channels(l, b, g, scale, out, inner, n, c, sp)
+        ctx.save_for_backward(*((inner, g) if inner is not None else (g,)))
+        ctx.needs_mag = inner is not None
+        ctx.scale = scale
+        ctx.dims = (n, c, sp)
+        ctx.mag_shape, ctx.mag_dtype = mag_norm_scale.shape, mag_norm_scale.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        if ctx.needs_mag:
+            inner, g = ctx.saved_tensors
+        else:
+            (g,) = ctx.saved_tensors
+            inner = None
+        n, c, sp = ctx.dims
+        d_out = d_out.contiguous()
+        need_l, need_b, need_m = ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.needs_input_grad[2]
+        d_lora = torch.empty_like(d_out) if need_l else None
+        d_base = torch.empty_like(d_out) if need_b else None
+        d_g = torch.empty(c, dtype=g.dtype, device=d_out.device) if (need_m and inner is not None) else None
+        if need_m and inner is None:
+            raise AssertionError("mag_norm_scale needs a gradient but inner was not saved")
+        if d_lora is not None or d_base is not None or d_g is not None:
+            _native.compose_bwd_channels(d_out, inner, g, ctx.scale, d_lora, d_base, d_g, n, c, sp)
+        d_mag = d_g.view(ctx.mag_shape).to(ctx.mag_dtype) if d_g is not None else None
+        return d_lora, d_base, d_mag, None
+
+
+def fused_dora_compose_channels(lora: torch.Tensor, base: torch.Tensor, mag_norm_scale: torch.Tensor,
+                                scale: float) -> torch.Tensor:
+    """out = (g - 1) * base + g * (scale * lora) with g per channel of [batch, channels, *spatial]
+    activations; differentiable in all three tensors."""
+    return FusedDoRAComposeChannelsFunction.apply(lora, base, mag_norm_scale, scale)

@@ -47,7 +47,34 @@ class DoraLinear(nn.Module):
             base_layer=self.base_layer, lora_A=self.lora_A.weight, lora_B=self.lora_B.weight, scaling=self.scaling
         )
 
+    @torch.no_grad()
+    def merge(self) -> None:
+        """Fold the adapter into the base weight (DoraLinearVariant.merge_unsafe,
+        variants.py:184-200); the forward is then the base layer alone."""
+        if getattr(self, "_merged_norm", None) is not None:
+            return
+        from .dora import merge_weight
+
+        merged, norm = merge_weight(self.base_layer.weight, self.lora_A.weight, self.lora_B.weight,
+                                    self.lora_magnitude_vector.weight, self.scaling)
+        self.base_layer.weight.copy_(merged)
+        self._merged_norm = norm
+
+    @torch.no_grad()
+    def unmerge(self) -> None:
+        """Restore the base weight (DoraLinearVariant.unmerge, variants.py:202-212)."""
+        norm = getattr(self, "_merged_norm", None)
+        if norm is None:
+            return
+        from .dora import unmerge_weight
+
+        self.base_layer.weight.copy_(unmerge_weight(self.base_layer.weight, self.lora_A.weight, self.lora_B.weight,
+                                                    self.lora_magnitude_vector.weight, norm, self.scaling))
+        self._merged_norm = None
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if getattr(self, "_merged_norm", None) is not None:
+            return self.base_layer(x)
         result = self.base_layer(x)
         if isinstance(self.lora_dropout, nn.Identity) or not self.training:
             # The common path: the DoRA delta and the add to the base output are one

@@ -142,6 +142,35 @@ int dora_linear_output_bwd(const void* d_y, const void* inner, const void* g, in
                            int64_t rows, int64_t cols, int act_dtype, void* stream);
 
 /*
+ * Compose forward for convolution outputs: activations [batch, channels,
+ * spatial] contiguous (spatial = the product of the spatial dims), g[channels]
+ * broadcast along the channel dimension.  out = (g-1)*base + g*(scale*lora)
+ * and, if inner is non-NULL, inner = scale*lora + base, per element exactly as
+ * dora_compose_fwd.  Out of place (out may not alias lora or base).
+ * Replaces the compose of _DoraConvNdLayer.forward
+ * (code/peft_patched/src/peft/tuners/lora/dora.py:1670-1715), which the
+ * reference evaluates on its eager path (g is not on the last dimension,
+ * dora_fused.py:563-574; eager formula dora.py:1331-1334).
+ */
+int dora_compose_fwd_channels(const void* lora, const void* base, const void* g, int g_dtype, double scale,
+                              void* out, void* inner, int64_t batch, int64_t channels, int64_t spatial,
+                              int act_dtype, void* stream);
+
+/* Workspace bytes of dora_compose_bwd_channels (per channel: a completion
+ * counter and one fp32 partial per batch split); zero it once before first use. */
+size_t dora_compose_bwd_channels_workspace_size(int64_t batch, int64_t channels, int64_t spatial, int act_dtype);
+
+/*
+ * Compose backward for convolution outputs (layout as above): d_lora =
+ * (g*scale)*d_out, d_base = (g-1)*d_out, d_g[c] = sum over batch and spatial
+ * of inner*d_out (deterministic), any subset.  Replaces the eager autograd of
+ * the conv compose (dora.py:1331-1334 under autograd).
+ */
+int dora_compose_bwd_channels(const void* d_out, const void* inner, const void* g, int g_dtype, double scale,
+                              void* d_lora, void* d_base, void* d_g, void* workspace, size_t workspace_bytes,
+                              int64_t batch, int64_t channels, int64_t spatial, int act_dtype, void* stream);
+
+/*
  * Size of the fixed device scratch array behind dora_compose_bwd_noalloc:
  * 4 MiB, held once on every GPU that loads the library.
  */

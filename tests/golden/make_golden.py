@@ -274,18 +274,174 @@ def gen_layer_cases(dora) -> dict:
     return out
 
 
+def gen_embedding_cases(dora) -> dict:
+    """``DoraEmbeddingLayer`` (dora.py:1491-1590) as ``DoraEmbeddingVariant`` drives it
+    (variants.py:287-379): init through ``update_layer`` with ``fan_in_fan_out=True``,
+    forward with the transposed adapter tensors and ``base_result = embedding(x)``,
+    y = result + delta, backward with a seeded upstream gradient."""
+    cases = {
+        # name: (tokens, vocab, dim, r, scale, dtype)
+        "emb_fp32": (20, 50, 64, 8, 2.0, "fp32"),
+        "emb_bf16": (24, 77, 96, 8, 0.5, "bf16"),
+    }
+    out = {}
+    for name, (T, V, d, r, s, dt) in cases.items():
+        g = torch.Generator().manual_seed(5000 + T + V + d + r)
+        tdt = _TORCH_DT[dt]
+        base = torch.nn.Embedding(V, d).to(tdt)
+        with torch.no_grad():
+            base.weight.copy_((torch.randn(V, d, generator=g) * 0.5).to(tdt))
+        base.weight.requires_grad_(False)
+        emb_A = torch.nn.Parameter((torch.randn(r, V, generator=g) * 0.3).to(tdt))  # lora_embedding_A [r, V]
+        emb_B = torch.nn.Parameter((torch.randn(d, r, generator=g) * 0.3).to(tdt))  # lora_embedding_B [d, r]
+        layer = dora.DoraEmbeddingLayer(fan_in_fan_out=True)
+        layer.update_layer(base_layer=base, lora_A=emb_A, lora_B=emb_B, scaling=s)
+        x = torch.randint(0, V, (T,), generator=g)
+        dy = torch.randn(T, d, generator=g).to(tdt)
+        embed_fn = lambda ids, w: torch.nn.functional.embedding(ids, w)  # noqa: E731
+        result = base(x)
+        _, delta = layer(x, lora_A=emb_A.T, lora_B=emb_B.T, scaling=s, base_layer=base, embed_fn=embed_fn,
+                         base_result=result)
+        if delta.dtype != result.dtype:
+            delta = delta.to(result.dtype)
+        y = result + delta
+        y.backward(dy)
+        st = {}
+        store_ids = x.to(torch.float32)  # token ids are small integers, exact in fp32
+        _put(st, "ids", store_ids)
+        _put(st, "W", base.weight)
+        _put(st, "A", emb_A)
+        _put(st, "B", emb_B)
+        _put(st, "m", layer.weight)
+        _put(st, "dy", dy)
+        _put(st, "y", y)
+        _put(st, "dA", emb_A.grad)
+        _put(st, "dB", emb_B.grad)
+        _put(st, "dm", layer.weight.grad)
+        _meta(st, scale=s, dtype=dt)
+        out[name] = st
+    return out
+
+
+def gen_conv_cases(dora) -> dict:
+    """``DoraConv1dLayer`` / ``DoraConv2dLayer`` (dora.py:1593-1742) the way PEFT's conv
+    LoRA wires them: lora_A = Conv(in, r, kernel, stride, padding), lora_B = Conv(r, out, 1),
+    ``base_result = base(x)`` (bias included; the layer subtracts it), y = result + delta,
+    backward with a seeded upstream gradient."""
+    cases = {
+        # name: (conv dims, batch, in, out, r, kernel, spatial, scale, dtype, bias)
+        "conv2d_fp32": (2, 3, 8, 12, 4, 3, 9, 2.0, "fp32", True),
+        "conv2d_bf16": (2, 2, 16, 24, 8, 3, 16, 0.5, "bf16", False),
+        "conv1d_fp32": (1, 4, 6, 10, 3, 5, 21, 1.0, "fp32", True),
+    }
+    out = {}
+    for name, (nd, N, ci, co, r, k, sp, s, dt, has_bias) in cases.items():
+        g = torch.Generator().manual_seed(6000 + N + ci + co + r + k + sp)
+        tdt = _TORCH_DT[dt]
+        Conv = torch.nn.Conv2d if nd == 2 else torch.nn.Conv1d
+        base = Conv(ci, co, k, padding=k // 2, bias=has_bias).to(tdt)
+        lora_A = Conv(ci, r, k, padding=k // 2, bias=False).to(tdt)
+        lora_B = Conv(r, co, 1, bias=False).to(tdt)
+        with torch.no_grad():
+            base.weight.copy_((torch.randn(base.weight.shape, generator=g) * 0.1).to(tdt))
+            if has_bias:
+                base.bias.copy_((torch.randn(co, generator=g) * 0.1).to(tdt))
+            lora_A.weight.copy_((torch.randn(lora_A.weight.shape, generator=g) * 0.1).to(tdt))
+            lora_B.weight.copy_((torch.randn(lora_B.weight.shape, generator=g) * 0.1).to(tdt))
+        base.weight.requires_grad_(False)
+        if has_bias:
+            base.bias.requires_grad_(False)
+        layer = (dora.DoraConv2dLayer if nd == 2 else dora.DoraConv1dLayer)(fan_in_fan_out=False)
+        layer.update_layer(base_layer=base, lora_A=lora_A.weight, lora_B=lora_B.weight, scaling=s)
+        shape = (N, ci) + (sp,) * nd
+        x = torch.randn(shape, generator=g).to(tdt).requires_grad_(True)
+        result = base(x)
+        dy = torch.randn(result.shape, generator=g).to(tdt)
+        delta = layer(x, lora_A=lora_A, lora_B=lora_B, scaling=s, base_layer=base, base_result=result)
+        if delta.dtype != result.dtype:
+            delta = delta.to(result.dtype)
+        y = result + delta
+        y.backward(dy)
+        st = {}
+        _put(st, "x", x)
+        _put(st, "W", base.weight)
+        if has_bias:
+            _put(st, "bias", base.bias)
+        _put(st, "A", lora_A.weight)
+        _put(st, "B", lora_B.weight)
+        _put(st, "m", layer.weight)
+        _put(st, "dy", dy)
+        _put(st, "y", y)
+        _put(st, "dx", x.grad)
+        _put(st, "dA", lora_A.weight.grad)
+        _put(st, "dB", lora_B.weight.grad)
+        _put(st, "dm", layer.weight.grad)
+        _meta(st, scale=s, dtype=dt, has_bias=int(has_bias), conv_dims=nd, kernel=k)
+        out[name] = st
+    return out
+
+
+def gen_merge_cases(dora) -> dict:
+    """DoRA merge / unmerge of a linear layer (variants.py:164-212): the dense
+    ``get_weight_norm(W, delta, 1)`` of the reference with delta = s * B A, then
+    W' = (m / norm) * (W + delta) and back W = W' / (m / norm) - delta.  The two
+    variant formulas are restated here (the variants module needs the rest of PEFT);
+    the norm is the reference's own ``get_weight_norm``."""
+    cases = {
+        # name: (out, in, r, scale, dtype)
+        "merge_fp32": (48, 40, 4, 2.0, "fp32"),
+        "merge_bf16": (64, 96, 8, 0.5, "bf16"),
+    }
+    out = {}
+    for name, (o, i, r, s, dt) in cases.items():
+        g = torch.Generator().manual_seed(7000 + o + i + r)
+        tdt = _TORCH_DT[dt]
+        W = (torch.randn(o, i, generator=g) * 0.05).to(tdt)
+        A = (torch.randn(r, i, generator=g) * 0.2).to(tdt)
+        B = (torch.randn(o, r, generator=g) * 0.2).to(tdt)
+        layer = dora.DoraLinearLayer(fan_in_fan_out=False)
+        base = torch.nn.Linear(i, o, bias=False).to(tdt)
+        with torch.no_grad():
+            base.weight.copy_(W)
+        layer.update_layer(base_layer=base, lora_A=A, lora_B=B, scaling=s)
+        with torch.no_grad():
+            layer.weight.mul_(1.05)  # a trained-looking magnitude
+            delta = (B @ A) * s
+            norm = layer.get_weight_norm(W, delta, scaling=1).detach()
+            factor = (layer.weight / norm).view(-1, 1)
+            merged = (factor * (W + delta)).to(tdt)
+            unmerged = (merged / factor - delta).to(tdt)
+        st = {}
+        _put(st, "W", W)
+        _put(st, "A", A)
+        _put(st, "B", B)
+        _put(st, "m", layer.weight.detach())
+        _put(st, "norm", norm)
+        _put(st, "merged", merged)
+        _put(st, "unmerged", unmerged)
+        _meta(st, scale=s, dtype=dt)
+        out[name] = st
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--groups", default="", help="comma-separated subset of groups to (re)write")
     args = ap.parse_args()
     torch.manual_seed(0)
     dora, dora_fused = import_reference(args.reference)
-    groups = {
-        "norm": gen_norm_cases(dora),
-        "compose": gen_compose_cases(dora, dora_fused),
-        "assembly": gen_assembly_cases(dora_fused),
-        "layer": gen_layer_cases(dora),
+    makers = {
+        "norm": lambda: gen_norm_cases(dora),
+        "compose": lambda: gen_compose_cases(dora, dora_fused),
+        "assembly": lambda: gen_assembly_cases(dora_fused),
+        "layer": lambda: gen_layer_cases(dora),
+        "embedding": lambda: gen_embedding_cases(dora),
+        "conv": lambda: gen_conv_cases(dora),
+        "merge": lambda: gen_merge_cases(dora),
     }
+    wanted = [g for g in args.groups.split(",") if g] or list(makers)
+    groups = {name: makers[name]() for name in wanted}
     for group, cases in groups.items():
         flat = {}
         for case, st in cases.items():
