@@ -598,6 +598,101 @@ def run_rowshard(args) -> None:
     dist.destroy_process_group()
 
 
+def run_model(args) -> None:
+    """Model-level configuration: a Llama-style decoder (hidden 4096, FFN 14336, 32
+    heads / 8 KV heads, vocab 128256; ``--layers`` of them, 32 by default) with DoRA
+    r=128, s=2.0 on q, k, v, o, gate, up and down, random weights; one sequence of
+    ``--seq`` random tokens per GPU (weak scaling), causal-LM loss, backward, DDP
+    all-reduce of the adapter gradients, fused AdamW step."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from dorafactors_b200 import _native
+    from dorafactors_b200.model import add_dora, build_llama, llama_config
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29512")
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=600),
+                                device_id=device)
+    cfg = llama_config(layers=args.layers)
+    model = build_llama(cfg, device)
+    params = add_dora(model, r=128, scaling=2.0)
+    runner = model
+    if world > 1:
+        runner = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank])
+    opt = torch.optim.AdamW(params, lr=1e-5, fused=True)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (1, args.seq), device=device, generator=g)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        loss = runner(input_ids=ids, labels=ids).loss
+        loss.backward()
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _native.launch_count()
+    e0.record()
+    for _ in range(args.steps):
+        loss = step()
+    e1.record()
+    torch.cuda.synchronize()
+    launches = (_native.launch_count() - launches0) // max(args.steps, 1) * args.steps
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    if rank == 0:
+        n_train = sum(p.numel() for p in params)
+        line = {
+            "metric": "DoRA model training tokens/s (Llama-style, 7 adapted projections per layer)",
+            "value": args.seq * world / (ms * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (random-init weights, uniform random token ids)",
+            "config": {"workload": f"llama-style decoder x{args.layers} (hidden 4096, ffn 14336, 32/8 heads, "
+                                   f"vocab 128256), DoRA r=128 s=2 on q,k,v,o,gate,up,down",
+                       "layers": args.layers, "global_batch": world, "seq_len": args.seq,
+                       "trainable_params": n_train, "parallelism": f"dp{world}",
+                       "l2": "activations far larger than L2, no flush needed"},
+            "loss": float(loss.detach()),
+            "gpu_launches": launches,
+            "clocks": clk,
+            "peak_mem_gb": torch.cuda.max_memory_allocated(device) / 1e9,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -605,8 +700,11 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core oracle sample")
-    ap.add_argument("--mode", choices=["dp", "rowshard"], default="dp",
-                    help="dp: token data parallelism (default); rowshard: out-feature sharding of one layer")
+    ap.add_argument("--mode", choices=["dp", "rowshard", "model"], default="dp",
+                    help="dp: token data parallelism (default); rowshard: out-feature sharding of one layer; "
+                         "model: Llama-style decoder with DoRA on every projection")
+    ap.add_argument("--layers", type=int, default=32, help="model mode: decoder layers")
+    ap.add_argument("--seq", type=int, default=4096, help="model mode: tokens per GPU")
     ap.add_argument("--shape", default="28672x8192", help="rowshard mode: out x in of the sharded layer")
     args = ap.parse_args(argv)
     if args.warmup < 3:
@@ -615,6 +713,8 @@ def main(argv=None) -> None:
         run_reference(args)
     elif args.mode == "rowshard":
         run_rowshard(args)
+    elif args.mode == "model":
+        run_model(args)
     else:
         run_native(args)
 
