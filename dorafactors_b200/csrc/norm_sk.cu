@@ -330,7 +330,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       const int64_t m = sg.m_tile * BM + row;
       cur_n0 = sg.n_tile * nt;
       const bool ssq_tile = sg.n_tile == 0;  // ||X||^2 once per row block
-      float ssq = 0.f;
+      float ssq8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight independent FMA chains
       bool ok = true;
       if (kSumSq) {
         for (int i = 0; i < sg.u_iters; ++i) {
@@ -353,7 +353,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const float x = to_f32(h[e]);
-              ssq = fmaf(x, x, ssq);
+              ssq8[e] = fmaf(x, x, ssq8[e]);
             }
           }
           __syncwarp();
@@ -373,7 +373,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       const float cacc = sg.u_iters > 0 ? rowdot_epilogue() : 0.f;
       if (m < a.M) {
         a.rowdot_part[(int64_t(slot) * a.n_tiles + sg.n_tile) * a.M + m] = cacc;
-        if (ssq_tile) a.sumsq_part[int64_t(slot) * a.M + m] = ssq;
+        if (ssq_tile) a.sumsq_part[int64_t(slot) * a.M + m] = sum8(ssq8);
       }
       float bacc = 0.f;
       if (sg.v_iters > 0) {

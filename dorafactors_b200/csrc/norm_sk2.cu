@@ -319,7 +319,7 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
       const Seg sg = segment(u);
       u = sg.tile * TU + sg.ub;
       const int64_t m = sg.tile * 2 * BM + int64_t(rank) * BM + row;
-      float ssq = 0.f;
+      float ssq8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight independent FMA chains
       bool ok = true;
       for (int i = 0; i < sg.u_iters; ++i) {
         const int64_t g = gk++;
@@ -333,7 +333,7 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float x = to_f32(h[e]);
-            ssq = fmaf(x, x, ssq);
+            ssq8[e] = fmaf(x, x, ssq8[e]);
           }
         }
         __syncwarp();
@@ -352,7 +352,7 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
       const float cacc = sg.u_iters > 0 ? rowdot_epilogue() : 0.f;
       if (m < a.M) {
         a.rowdot_part[int64_t(slot) * a.M + m] = cacc;
-        a.sumsq_part[int64_t(slot) * a.M + m] = ssq;
+        a.sumsq_part[int64_t(slot) * a.M + m] = sum8(ssq8);
       }
       float bacc = 0.f;
       if (sg.v_iters > 0) {

@@ -251,7 +251,7 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const int64_t m = m0 + row;
-    float ssq = 0.f;
+    float ssq8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight independent FMA chains
     if (do_ssq) {
       for (int it = 0; it < iters; ++it) {
         const int s = it % stages, round = it / stages;
@@ -265,7 +265,7 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float x = to_f32(h[e]);
-            ssq = fmaf(x, x, ssq);
+            ssq8[e] = fmaf(x, x, ssq8[e]);
           }
         }
         __syncwarp();
@@ -308,7 +308,7 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
         const float acc = rowdot_epilogue();
         if (m < a.M) {
           a.rowdot_part[(int64_t(ks) * a.n_tiles + n_tile) * a.M + m] = acc;
-          if (do_ssq) a.sumsq_part[int64_t(ks) * a.M + m] = ssq;
+          if (do_ssq) a.sumsq_part[int64_t(ks) * a.M + m] = sum8(ssq8);
         }
         if (v_iters > 0) {
           // Hand the TMEM columns to the fused phase, then contract its product.
