@@ -274,3 +274,58 @@ def dora_linear_forward_backward(x, W, bias, A, B, m, scale: float, dy, dtype: s
     dA = _matmul(d_xa.T, x, dtype)
     dx = _op(np.add, dtype, _matmul(d_res, W, dtype), _matmul(d_xa, A, dtype))
     return {"y": y, "delta": delta, "norm": norm, "g": g, "dx": dx, "dA": dA, "dB": dB, "dm": dm}
+
+
+# ---------------------------------------------------------------------------
+# Convolution / embedding norms and merge (the next rows beside the linear path)
+# ---------------------------------------------------------------------------
+def weight_norm_conv(W, A, B, scale: float, dtype: str):
+    """``_DoraConvNdLayer._get_weight_norm_conv_factored`` (dora.py:1594-1634): the
+    linear factored norm on the flattened weights ``W [out, -1]``, ``A [r, -1]``,
+    ``B [out, -1]`` (a grouped B, ``[out, r/groups]``, expanded block-diagonally),
+    returned as ``[1, out, 1, ...]``."""
+    W = np.asarray(W, np.float32)
+    out = W.shape[0]
+    r = np.asarray(A).shape[0]
+    fw = W.reshape(out, -1)
+    fa = np.asarray(A, np.float32).reshape(r, -1)
+    fb = np.asarray(B, np.float32).reshape(out, -1)
+    rpg = fb.shape[1]
+    if rpg > 0 and r % rpg == 0 and r // rpg > 1 and out % (r // rpg) == 0:
+        groups = r // rpg
+        opg = out // groups
+        e = np.zeros((out, r), np.float32)
+        for gi in range(groups):
+            e[gi * opg:(gi + 1) * opg, gi * rpg:(gi + 1) * rpg] = fb[gi * opg:(gi + 1) * opg]
+        fb = e
+    n, _ = weight_norm_factored(fw, fa, fb, scale, dtype)
+    return n.reshape((1, out) + (1,) * (W.ndim - 2))
+
+
+def weight_norm_embedding(table, emb_A, emb_B, scale: float, dtype: str):
+    """Embedding DoRA magnitude (``DoraEmbeddingVariant.init`` -> ``update_layer`` with
+    ``fan_in_fan_out=True``, variants.py:287-300, dora.py:1341-1378): one value per
+    embedding dimension, ``||table[:, j] + s (emb_A^T emb_B^T)[:, j]||`` over the
+    vocabulary, i.e. the factored norm of ``W0 = table^T``, ``A = emb_A``, ``B = emb_B``."""
+    return weight_norm_factored(table, emb_A, emb_B, scale, dtype, fan_in_fan_out=True)[0]
+
+
+def compose_channels(lora, base, g, scale: float, dtype: str) -> np.ndarray:
+    """Eager compose with g per channel of ``[N, C, *spatial]`` activations
+    (dora.py:1331-1334 with ``mag_norm_scale`` shaped ``[1, C, 1, ...]``)."""
+    lora = np.asarray(lora, np.float32)
+    gb = np.asarray(g, np.float32).reshape((1, -1) + (1,) * (lora.ndim - 2))
+    sl = _op(np.multiply, dtype, np.float32(scale), lora)
+    a = _op(np.multiply, dtype, gb - np.float32(1), base)
+    return _op(np.add, dtype, a, _op(np.multiply, dtype, gb, sl))
+
+
+def merge_weight(W, A, B, m, scale: float, dtype: str):
+    """``DoraLinearVariant.merge_safe`` (variants.py:164-182): delta = s B A,
+    norm = ``get_weight_norm(W, delta, 1)``, ``W' = (m / norm) (W + delta)`` in the
+    weight dtype.  Returns ``(merged, norm)``."""
+    delta = np.asarray(B, np.float32) @ np.asarray(A, np.float32) * np.float32(scale)
+    norm = weight_norm_dense(W, delta, 1.0, dtype)
+    factor = (np.asarray(m, np.float32) / norm)[:, None]
+    merged = round_to(factor * (np.asarray(W, np.float32) + delta), dtype)
+    return merged, norm

@@ -76,6 +76,16 @@ def test_argument_validation_without_gpu(lib):
     assert lib.dora_weight_norm(None, None, None, 0, 8, 4, 2, 2, 2, 1.0, None, None, None, 0, s) == 0
     assert lib.dora_norm_assembly(None, None, None, 1.0, None, 0, s) == 0
     assert lib.dora_norm_assembly(None, None, None, 1.0, None, -3, s) == 1
+    # Channel-layout compose: bad sizes / dtypes, in-place and aliasing refused, empty is a no-op.
+    assert lib.dora_compose_fwd_channels(vp(16), vp(32), vp(48), 2, 1.0, vp(64), None, -1, 4, 8, 2, s) == 1
+    assert lib.dora_compose_fwd_channels(vp(16), vp(32), vp(48), 1, 1.0, vp(64), None, 2, 4, 8, 2, s) == 1
+    assert lib.dora_compose_fwd_channels(vp(16), vp(32), vp(48), 2, 1.0, vp(16), None, 2, 4, 8, 2, s) == 1
+    assert lib.dora_compose_fwd_channels(vp(16), vp(32), vp(48), 2, 1.0, vp(64), vp(32), 2, 4, 8, 2, s) == 1
+    assert lib.dora_compose_fwd_channels(None, None, None, 2, 1.0, None, None, 0, 4, 8, 2, s) == 0
+    assert lib.dora_compose_bwd_channels(vp(16), None, vp(48), 2, 1.0, None, None, vp(64), None, 0, 2, 4, 8, 2,
+                                         s) == 1
+    assert lib.dora_compose_bwd_channels(vp(16), vp(32), vp(48), 2, 1.0, None, None, None, None, 0, 0, 4, 8, 2,
+                                         s) == 0
 
 
 def test_workspace_sizes(lib):
@@ -89,6 +99,9 @@ def test_workspace_sizes(lib):
     assert n1 > 0 and n2 > 0
     # O(out + r^2) floats, independent of in_features beyond the split count.
     assert n1 < 64 * 2**20
+    c = lib.dora_compose_bwd_channels_workspace_size(32, 256, 784, 2)
+    assert c >= 256 * 4 + 256 * 4 and c % 4 == 0
+    assert lib.dora_compose_bwd_channels_workspace_size(32, 0, 784, 2) == 0
 
 
 def test_build_is_cached():

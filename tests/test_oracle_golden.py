@@ -100,3 +100,29 @@ def test_layer_forward_backward(case):
     tol = RTOL[dt]
     for k in ("y", "delta", "norm", "dx", "dA", "dB", "dm"):
         assert_close(r[k], st[k], tol, f"{case} {k}")
+
+
+# ---------------------------------------------------------------------------
+# Next rows: conv / embedding norms and the merge, against the reference's fixtures
+# ---------------------------------------------------------------------------
+def test_oracle_conv_norm_golden():
+    for case, st in load_group("conv").items():
+        dt = st["dtype"]
+        n = orc.weight_norm_conv(st["W"], st["A"], st["B"], float(st["scale"]), dt)
+        assert n.shape == st["m"].shape, case
+        assert_close(n, st["m"], 1e-6 if dt == "fp32" else 8e-3, f"{case} magnitude at init")
+
+
+def test_oracle_embedding_norm_golden():
+    for case, st in load_group("embedding").items():
+        dt = st["dtype"]
+        n = orc.weight_norm_embedding(st["W"], st["A"], st["B"], float(st["scale"]), dt)
+        assert_close(n, st["m"], 1e-6 if dt == "fp32" else 8e-3, f"{case} magnitude at init")
+
+
+def test_oracle_merge_golden():
+    for case, st in load_group("merge").items():
+        dt = st["dtype"]
+        merged, norm = orc.merge_weight(st["W"], st["A"], st["B"], st["m"], float(st["scale"]), dt)
+        assert_close(norm, st["norm"], 1e-6 if dt == "fp32" else 8e-3, f"{case} norm")
+        assert_close(merged, st["merged"], 1e-6 if dt == "fp32" else 8e-3, f"{case} merged")
