@@ -64,6 +64,10 @@ __host__ __device__ inline uint32_t sk_stage_bytes(int nt) { return kXTileBytes 
 // narrow enough) a separate region for the staged Z rows and two G slots, so
 // the next segment's ring loads can stream in while this segment's epilogue
 // runs; wide tiles stage Z / G in the idle ring instead.
+// Narrow tiles (small r) stream W0 with up to 12 stages in flight: at r = 16 a stage
+// is 18 KB, and more bytes in flight per SM is what the HBM stream needs.
+constexpr int kMaxSkStages = 12;
+
 struct SkLayout {
   int stages, apart;
   uint32_t stage_off, bar_off, total;
@@ -75,7 +79,7 @@ inline SkLayout sk_layout(int nt, bool fuse_v) {
   const uint32_t staging = z_bytes + (fuse_v ? 2u * uint32_t(nt) * 128u : 0u);
   SkLayout L{};
   int s_apart = staging < budget ? int((budget - staging) / stage) : 0;
-  if (s_apart > 8) s_apart = 8;
+  if (s_apart > kMaxSkStages) s_apart = kMaxSkStages;
   if (s_apart >= 4) {
     L.stages = s_apart;
     L.apart = 1;
@@ -83,12 +87,12 @@ inline SkLayout sk_layout(int nt, bool fuse_v) {
     L.bar_off = L.stage_off + staging;
   } else {
     int s = int(budget / stage);
-    L.stages = s > 8 ? 8 : s;
+    L.stages = s > kMaxSkStages ? kMaxSkStages : s;
     L.apart = 0;
     L.stage_off = 0;
     L.bar_off = stage * uint32_t(L.stages);
   }
-  L.total = 1024u + L.bar_off + 256u;
+  L.total = 1024u + L.bar_off + 512u;  // barriers (2 per stage + 10) and two words
   return L;
 }
 
@@ -456,7 +460,7 @@ SkPlan tc_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
 
 template <typename T, bool SSQ>
 static int launch_sk(const tc::SkArgs& k, const CUtensorMap* m, cudaStream_t st) {
-  const uint32_t smem = 1024u + k.bar_off + 256u;
+  const uint32_t smem = 1024u + k.bar_off + 512u;
   auto kfn = tc::tc_sk_rowdot_kernel<T, SSQ>;
   static std::atomic<unsigned long long> opted{0};
   int dev = 0;
