@@ -39,6 +39,7 @@ SIGNATURES = {
     "dora_compose_fwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _int, _vp]),
     "dora_compose_bwd_workspace_size": (_sz, [_i64, _i64, _int]),
     "dora_compose_bwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
+    "dora_selftest_bounded_wait": (_int, [ctypes.c_longlong, ctypes.POINTER(ctypes.c_int), _vp]),
     "dora_compose_fwd_channels": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "dora_compose_bwd_channels_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "dora_compose_bwd_channels": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _i64,

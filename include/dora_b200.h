@@ -67,6 +67,16 @@ unsigned long long dora_launch_count(void);
 int dora_device_error(int reset, int* out);
 
 /*
+ * Self-test of the bounded device-side waits (no counterpart in the reference,
+ * whose Triton kernels have no cross-warp waits): launches one thread that
+ * waits, with a limit of `limit_cycles` SM cycles (1 .. about 2^31), on an
+ * mbarrier phase that never completes.  It must give up, set
+ * DORA_ERR_DEVICE_TIMEOUT in the device error word (read it with
+ * dora_device_error) and return; *gave_up is 1 then.  Synchronises `stream`.
+ */
+int dora_selftest_bounded_wait(long long limit_cycles, int* gave_up, void* stream);
+
+/*
  * Fused compose forward.
  *   out[i,j]   = (g[j] - 1) * base[i,j] + g[j] * (scale * lora[i,j])
  *   inner[i,j] = scale * lora[i,j] + base[i,j]            (only if inner != NULL)
