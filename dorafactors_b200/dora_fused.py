@@ -58,6 +58,16 @@ def _mag_broadcasts_last_dim(mag: torch.Tensor, lora: torch.Tensor) -> bool:
     return mag.ndim > 0 and lora.ndim > 0 and mag.numel() == lora.shape[-1] and mag.shape[-1] == lora.shape[-1]
 
 
+def _mag_is_per_channel(mag: torch.Tensor, lora: torch.Tensor) -> bool:
+    """True for the convolution layout: *lora* is [batch, C, *spatial] and *mag* is
+    [1, C, 1, ...] of the same rank (the g of _DoraConvNdLayer.forward, dora.py:1670-1715),
+    and the last-dim layout does not apply.  The reference sends this case to its
+    PyTorch fallback (dora_fused.py:563-574); here it runs the channel-layout kernels."""
+    if lora.ndim < 3 or mag.ndim != lora.ndim or _mag_broadcasts_last_dim(mag, lora):
+        return False
+    return mag.shape[1] == lora.shape[1] and all(mag.shape[i] == 1 for i in range(mag.ndim) if i != 1)
+
+
 def _prepare(lora: torch.Tensor, base: torch.Tensor, mag: torch.Tensor, what: str):
     """Validate and normalise operands: 2-D contiguous activations of one dtype and a
     contiguous 1-D ``g`` in the activation dtype or fp32."""
@@ -99,6 +109,12 @@ def fused_dora_compose(
     buffer), otherwise a new tensor of ``lora``'s shape and dtype is returned.
     """
     orig = lora
+    if _mag_is_per_channel(mag_norm_scale, lora):
+        out, _ = _channels_forward(lora, base, mag_norm_scale, scale, False, "fused_dora_compose")
+        if inplace:
+            orig.copy_(out)
+            return orig
+        return out
     l, b, g, rows, cols = _prepare(lora, base, mag_norm_scale, "fused_dora_compose")
     if inplace:
         out = l  # contiguous view of lora, or a contiguous copy written back below
@@ -121,6 +137,8 @@ def fused_dora_forward_and_inner(
 ) -> tuple:
     """``(out, inner)`` in one pass: out as in ``fused_dora_compose``, inner = s * lora + base
     (dora_fused.py:674-772).  ``scale * lora`` never leaves registers."""
+    if _mag_is_per_channel(mag_norm_scale, lora):
+        return _channels_forward(lora, base, mag_norm_scale, scale, True, "fused_dora_forward_and_inner")
     l, b, g, rows, cols = _prepare(lora, base, mag_norm_scale, "fused_dora_forward_and_inner")
     out = torch.empty_like(l)
     inner = torch.empty_like(l)
@@ -154,6 +172,8 @@ def fused_norm_assembly(
 
 def _backward(d_out, inner, mag, scale, need_lora, need_base, need_mag):
     """Native fused backward; returns (d_lora, d_base, d_mag) shaped like the inputs."""
+    if _mag_is_per_channel(mag, d_out):
+        return _channels_backward(d_out, inner, mag, scale, need_lora, need_base, need_mag)
     _native.require_cuda(d_out, inner, mag, what="FusedDoRAComposeFunction.backward")
     cols = d_out.shape[-1]
     rows = d_out.numel() // cols if cols else 0
@@ -433,42 +453,69 @@ def _prepare_channels(lora: torch.Tensor, base: torch.Tensor, mag: torch.Tensor,
     return lora.contiguous(), base.contiguous(), g.contiguous(), batch, channels, spatial
 
 
+def _channels_forward(lora, base, mag, scale, with_inner: bool, what: str):
+    """Conv-layout ``(out, inner or None)``: new tensors shaped like ``lora``."""
+    l, b, g, n, c, sp = _prepare_channels(lora, base, mag, what)
+    out = torch.empty_like(l)
+    inner = torch.empty_like(l) if with_inner else None
+    if out.numel():
+        _native.compose_fwd_channels(l, b, g, scale, out, inner, n, c, sp)
+    return out, inner
+
+
+def _channels_backward(d_out, inner, mag, scale, need_lora, need_base, need_mag):
+    """Conv-layout backward: (d_lora, d_base, d_mag) with d_mag shaped and typed like ``mag``."""
+    _native.require_cuda(d_out, inner, mag, what="fused_dora_compose_channels backward")
+    if d_out.ndim < 2:
+        raise ValueError(f"expected [batch, channels, *spatial] gradients, got {tuple(d_out.shape)}")
+    n, c = d_out.shape[0], d_out.shape[1]
+    sp = d_out.numel() // (n * c) if n and c else 0
+    if mag.numel() != c:
+        raise ValueError(f"mag_norm_scale {tuple(mag.shape)} does not hold one value per channel ({c})")
+    act = d_out.dtype
+    g = mag.reshape(-1)
+    if g.dtype not in (act, torch.float32):
+        g = g.float()
+    g = g.contiguous()
+    d = d_out.contiguous()
+    if need_mag and inner is None:
+        raise AssertionError("mag_norm_scale needs a gradient but inner was not saved")
+    inn = None
+    if need_mag:
+        inn = (inner if inner.dtype == act else inner.to(act)).contiguous()
+    d_lora = torch.empty_like(d) if need_lora else None
+    d_base = torch.empty_like(d) if need_base else None
+    d_g = torch.empty(c, dtype=g.dtype, device=d.device) if need_mag else None
+    if d.numel() and (need_lora or need_base or need_mag):
+        _native.compose_bwd_channels(d, inn, g, scale, d_lora, d_base, d_g, n, c, sp)
+    elif d_g is not None:
+        d_g.zero_()
+    d_mag = d_g.view(mag.shape).to(mag.dtype) if d_g is not None else None
+    return d_lora, d_base, d_mag
+
+
 class FusedDoRAComposeChannelsFunction(torch.autograd.Function):
     """Conv-layout compose with the native fused backward; saves ``inner`` only when
     the magnitude needs a gradient, like ``FusedDoRAComposeFunction``."""
 
     @staticmethod
     def forward(ctx, lora, base, mag_norm_scale, scale):
-        l, b, g, n, c, sp = _prepare_channels(lora, base, mag_norm_scale, "fused_dora_compose_channels")
-        out = torch.empty_like(l)
-        inner = torch.empty_like(l) if mag_norm_scale.requires_grad else None
-        if out.numel():
-            _native.compose_fwd_channels(l, b, g, scale, out, inner, n, c, sp)
-        ctx.save_for_backward(*((inner, g) if inner is not None else (g,)))
-        ctx.needs_mag = inner is not None
+        needs_mag = mag_norm_scale.requires_grad
+        out, inner = _channels_forward(lora, base, mag_norm_scale, scale, needs_mag, "fused_dora_compose_channels")
+        ctx.save_for_backward(*((inner, mag_norm_scale) if needs_mag else (mag_norm_scale,)))
+        ctx.needs_mag = needs_mag
         ctx.scale = scale
-        ctx.dims = (n, c, sp)
-        ctx.mag_shape, ctx.mag_dtype = mag_norm_scale.shape, mag_norm_scale.dtype
         return out
 
     @staticmethod
     def backward(ctx, d_out):
         if ctx.needs_mag:
-            inner, g = ctx.saved_tensors
+            inner, mag = ctx.saved_tensors
         else:
-            (g,) = ctx.saved_tensors
+            (mag,) = ctx.saved_tensors
             inner = None
-        n, c, sp = ctx.dims
-        d_out = d_out.contiguous()
-        need_l, need_b, need_m = ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.needs_input_grad[2]
-        d_lora = torch.empty_like(d_out) if need_l else None
-        d_base = torch.empty_like(d_out) if need_b else None
-        d_g = torch.empty(c, dtype=g.dtype, device=d_out.device) if (need_m and inner is not None) else None
-        if need_m and inner is None:
-            raise AssertionError("mag_norm_scale needs a gradient but inner was not saved")
-        if d_lora is not None or d_base is not None or d_g is not None:
-            _native.compose_bwd_channels(d_out, inner, g, ctx.scale, d_lora, d_base, d_g, n, c, sp)
-        d_mag = d_g.view(ctx.mag_shape).to(ctx.mag_dtype) if d_g is not None else None
+        d_lora, d_base, d_mag = _channels_backward(d_out, inner, mag, ctx.scale, ctx.needs_input_grad[0],
+                                                   ctx.needs_input_grad[1], ctx.needs_input_grad[2])
         return d_lora, d_base, d_mag, None
 
 

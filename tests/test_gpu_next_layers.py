@@ -164,3 +164,46 @@ def test_channel_compose_kernels(dtype, gdt, N, C, S):
     d_g2 = torch.empty_like(d_g)
     _native.compose_bwd_channels(d_out, inner, g, s, None, None, d_g2, N, C, S)
     assert torch.equal(d_g, d_g2)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
+def test_reference_api_with_per_channel_magnitude(dtype):
+    """The reference-facing compose functions given a convolution-layout magnitude
+    ([1, C, 1, 1] on [N, C, H, W] activations; the reference evaluates that case with its
+    PyTorch fallback, dora_fused.py:563-574) run the channel kernels: outputs and all
+    gradients against a PyTorch fp32 evaluation."""
+    from dorafactors_b200 import dora_fused as F
+
+    td = {"bf16": torch.bfloat16, "fp32": torch.float32}[dtype]
+    tol = RTOL[dtype]
+    torch.manual_seed(11)
+    N, C, H, W = 3, 24, 5, 7
+    lora = torch.randn(N, C, H, W, device="cuda").to(td)
+    base = torch.randn(N, C, H, W, device="cuda").to(td)
+    mag = (torch.rand(1, C, 1, 1, device="cuda") + 0.5).to(td)
+    s = 0.75
+    mf, lf, bf = mag.float(), lora.float(), base.float()
+    ref = (mf - 1) * bf + mf * (s * lf)
+    ref_inner = s * lf + bf
+    assert_close(to_np(F.fused_dora_compose(lora, base, mag, s, inplace=False)), to_np(ref), tol, "out-of-place")
+    l2 = lora.clone()
+    r = F.fused_dora_compose(l2, base, mag, s, inplace=True)
+    assert r.data_ptr() == l2.data_ptr()
+    assert_close(to_np(l2), to_np(ref), tol, "in place")
+    out, inner = F.fused_dora_forward_and_inner(lora, base, mag, s)
+    assert_close(to_np(out), to_np(ref), tol, "forward_and_inner out")
+    assert_close(to_np(inner), to_np(ref_inner), tol, "forward_and_inner inner")
+    dy = torch.randn(N, C, H, W, device="cuda").to(td)
+    dyf = dy.float()
+    for name, fn in (("FusedDoRAComposeFunction", F.FusedDoRAComposeFunction.apply),
+                     ("fused_dora_compose_autograd", F.fused_dora_compose_autograd)):
+        l = lora.clone().requires_grad_(True)
+        b = base.clone().requires_grad_(True)
+        m = mag.clone().requires_grad_(True)
+        y = fn(l, b, m, s)
+        assert_close(to_np(y), to_np(ref), tol, f"{name} out")
+        y.backward(dy)
+        assert m.grad.shape == mag.shape and m.grad.dtype == mag.dtype
+        assert_close(to_np(l.grad), to_np(mf * s * dyf), tol, f"{name} d_lora")
+        assert_close(to_np(b.grad), to_np((mf - 1) * dyf), tol, f"{name} d_base")
+        assert_close(to_np(m.grad), to_np((ref_inner * dyf).sum(dim=(0, 2, 3), keepdim=True)), tol, f"{name} d_mag")

@@ -68,6 +68,33 @@ def test_mag_shape_rules():
     assert not _mag_broadcasts_last_dim(torch.empty(()), lora)
 
 
+def test_per_channel_magnitude_rule():
+    """The convolution layout ([1, C, 1, ...] on [batch, C, *spatial]) is recognised and
+    routed to the channel kernels; last-dim vectors and other broadcasts are not."""
+    from dorafactors_b200.dora_fused import _mag_is_per_channel
+
+    x4 = torch.empty(2, 6, 5, 7)
+    assert _mag_is_per_channel(torch.empty(1, 6, 1, 1), x4)
+    assert _mag_is_per_channel(torch.empty(1, 6, 1), torch.empty(3, 6, 9))
+    assert not _mag_is_per_channel(torch.empty(7), x4)  # last-dim layout
+    assert not _mag_is_per_channel(torch.empty(1, 1, 1, 7), x4)
+    assert not _mag_is_per_channel(torch.empty(6), x4)  # rank differs: not the conv layout
+    assert not _mag_is_per_channel(torch.empty(1, 6, 5, 1), x4)
+    assert not _mag_is_per_channel(torch.empty(1, 6), torch.empty(4, 6))  # 2-D: linear layout
+
+
+def test_per_channel_magnitude_on_cpu_fails_loudly():
+    from dorafactors_b200 import dora_fused as df
+
+    x = torch.randn(2, 6, 5, 7)
+    g = torch.ones(1, 6, 1, 1)
+    for fn in (lambda: df.fused_dora_compose(x, x.clone(), g, 1.0),
+               lambda: df.fused_dora_compose(x.clone(), x, g, 1.0, inplace=False),
+               lambda: df.fused_dora_forward_and_inner(x, x.clone(), g, 1.0)):
+        with pytest.raises(RuntimeError, match="CUDA"):
+            fn()
+
+
 def test_dtype_codes_match_header():
     import re
 
