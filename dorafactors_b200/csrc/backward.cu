@@ -230,16 +230,18 @@ static int bwd_entry(const void* d_out, const void* inner, const void* g, int g_
   if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
   if (g_dtype != act_dtype && g_dtype != DORA_DTYPE_F32) return DORA_ERR_INVALID_ARGUMENT;
   if (!d_lora && !d_base && !d_g) return DORA_OK;
-  if (d_g && !inner) return DORA_ERR_INVALID_ARGUMENT;
-  if (!d_out || !g) return DORA_ERR_INVALID_ARGUMENT;
   if (rows == 0 || cols == 0) {
-    // Empty activations: the column sums are zero.
+    // Empty activations (their pointers may be null, as PyTorch gives for zero
+    // elements): the column sums are zero, the reference's result for an empty
+    // batch (test_dora_fused.py TestEdgeCases, empty-tensor backward).
     if (d_g && cols > 0) {
       cudaError_t e = cudaMemsetAsync(d_g, 0, size_t(cols) * dtype_size(g_dtype), static_cast<cudaStream_t>(stream));
       if (e != cudaSuccess) return set_cuda_error(e);
     }
     return DORA_OK;
   }
+  if (d_g && !inner) return DORA_ERR_INVALID_ARGUMENT;
+  if (!d_out || !g) return DORA_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float s = float(scale);
   switch (act_dtype) {

@@ -109,7 +109,8 @@ size_t dora_compose_bwd_workspace_size(int64_t rows, int64_t cols, int act_dtype
  * d_lora / d_base are in act_dtype, d_g in g_dtype.  The column sum runs in
  * fp32 in a fixed order (per-thread, then CTA tree, then per-CTA partials
  * folded by the last CTA of each column tile), so results are deterministic.
- * inner is required iff d_g != NULL.
+ * inner is required iff d_g != NULL and rows * cols > 0.  With rows == 0 the
+ * activation pointers may be NULL and d_g (if given) is set to zero.
  *
  * Replaces FusedDoRAComposeFunction.backward / _fused_backward_triton
  * (dora_fused.py:1137-1206, 1264-1344, kernel 1010-1062), including the

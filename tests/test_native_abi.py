@@ -70,6 +70,9 @@ def test_argument_validation_without_gpu(lib):
     # Backward: d_g requires inner; nothing requested is a no-op.
     assert lib.dora_compose_bwd(vp(16), None, vp(48), 2, 1.0, None, None, vp(64), None, 0, 4, 8, 2, s) == 1
     assert lib.dora_compose_bwd(vp(16), vp(32), vp(48), 2, 1.0, None, None, None, None, 0, 4, 8, 2, s) == 0
+    # Zero rows: the (empty) activations may be NULL pointers, as PyTorch hands them over.
+    assert lib.dora_compose_bwd(None, None, vp(48), 2, 1.0, vp(96), vp(128), None, None, 0, 0, 8, 2, s) == 0
+    assert lib.dora_linear_output_bwd(None, None, vp(48), 2, 1.0, vp(96), vp(128), None, None, 0, 0, 8, 2, s) == 0
     # Norm: bad sizes / dtypes.
     assert lib.dora_weight_norm(vp(16), vp(32), vp(48), -1, 8, 4, 2, 2, 2, 1.0, vp(64), None, None, 0, s) == 1
     assert lib.dora_weight_norm(vp(16), vp(32), vp(48), 4, 8, 4, 2, 9, 2, 1.0, vp(64), None, None, 0, s) == 1
