@@ -147,3 +147,81 @@ def test_d_mag_across_scales_vs_fp64(scale):
     torch.testing.assert_close(dm.double(), m64.grad, rtol=1e-5, atol=1e-5)
     torch.testing.assert_close(dl.double(), l64.grad, rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(db.double(), b64.grad, rtol=1e-5, atol=1e-6)
+
+
+def test_near_zero_norm_stays_finite():
+    """Norm components that cancel to ~0: the assembled norm is >= 0 and m / clamp(norm)
+    is finite (test_dora_fused.py TestFusedNormAssemblyNearZero)."""
+    from dorafactors_b200 import dora_fused as F
+
+    n = 32
+    w = torch.full((n,), 1e-12, device="cuda")
+    (norm,) = F.fused_norm_assembly(w, -w, w, 0.5)
+    assert (norm >= 0).all()
+    mag = torch.rand(n, device="cuda") + 0.1
+    assert torch.isfinite(mag / norm.clamp_min(1e-6)).all()
+
+
+def _layer(seed=903, in_f=32, out_f=16, r=4, scaling=0.5):
+    from dorafactors_b200.dora import DoraLinearLayer
+
+    torch.manual_seed(seed)
+    base = torch.nn.Linear(in_f, out_f, bias=True, device="cuda")
+    base.requires_grad_(False)
+    lora_A = torch.nn.Linear(in_f, r, bias=False, device="cuda")
+    lora_B = torch.nn.Linear(r, out_f, bias=False, device="cuda")
+    with torch.no_grad():
+        lora_B.weight.normal_(0.0, 0.1)
+    layer = DoraLinearLayer(fan_in_fan_out=False)
+    layer.update_layer(base_layer=base, lora_A=lora_A.weight, lora_B=lora_B.weight, scaling=scaling)
+    return base, lora_A, lora_B, layer
+
+
+def _step(base, lora_A, lora_B, layer, x, scaling=0.5):
+    out = layer(x, lora_A=lora_A, lora_B=lora_B, scaling=scaling, base_layer=base, base_result=base(x).detach())
+    out.sum().backward()
+
+
+def test_gradient_accumulation_equals_sum_of_passes():
+    """Three passes without zeroing the gradients give the sum of the three single-pass
+    gradients of A, B and the magnitude (TestGradientAccumulationCorrectness)."""
+    xs = [_f(4, 32, seed=904 + i) for i in range(3)]
+    acc = _layer()
+    for x in xs:
+        _step(*acc, x)
+    ind = _layer()
+    sums = [torch.zeros_like(p) for p in (ind[1].weight, ind[2].weight, ind[3].weight)]
+    for x in xs:
+        for p in (ind[1].weight, ind[2].weight, ind[3].weight):
+            p.grad = None
+        _step(*ind, x)
+        for s_, p in zip(sums, (ind[1].weight, ind[2].weight, ind[3].weight)):
+            s_ += p.grad
+    for name, got, want in zip(("A", "B", "magnitude"), (acc[1].weight.grad, acc[2].weight.grad, acc[3].weight.grad),
+                               sums):
+        assert (got - want).abs().max().item() <= 1e-5, name
+
+
+def test_no_device_memory_growth_across_steps():
+    """Forward + backward repeated: allocated device memory does not grow after warm-up
+    (workspaces are cached per device, stream and kind, not per call)."""
+    import gc
+
+    base, lora_A, lora_B, layer = _layer(seed=906, in_f=64, out_f=32, r=8)
+    params = (lora_A.weight, lora_B.weight, layer.weight)
+
+    def cycle():
+        _step(base, lora_A, lora_B, layer, torch.randn(8, 64, device="cuda"))
+        for p in params:
+            p.grad = None
+
+    for _ in range(10):
+        cycle()
+    gc.collect()
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    for _ in range(40):
+        cycle()
+    gc.collect()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() <= before * 1.1 + 1024
