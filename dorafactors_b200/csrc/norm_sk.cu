@@ -342,7 +342,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
           const int s = int(g % S);
           // Every ring use is released by the row warps too (fixed barrier count); the
           // data is summed only in the N tile that owns ||X||^2.
-          if (!__all_sync(0xffffffffu, mbar_wait(&full[s], uint32_t((g / S) & 1)))) { ok = false; break; }
+          if (!warp_wait(&full[s], uint32_t((g / S) & 1))) { ok = false; break; }
           if (!ssq_tile) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);

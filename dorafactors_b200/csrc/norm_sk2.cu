@@ -324,7 +324,7 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
       for (int i = 0; i < sg.u_iters; ++i) {
         const int64_t g = gk++;
         const int s = int(g % S);
-        if (!__all_sync(0xffffffffu, mbar_wait(&mdone[s], uint32_t((g / S) & 1)))) { ok = false; break; }
+        if (!warp_wait(&mdone[s], uint32_t((g / S) & 1))) { ok = false; break; }
         const uint8_t* rowp = base + size_t(s) * stage_bytes + row * 128;
 #pragma unroll
         for (int p = 0; p < 8; ++p) {

@@ -255,7 +255,7 @@ tc_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
     if (do_ssq) {
       for (int it = 0; it < iters; ++it) {
         const int s = it % stages, round = it / stages;
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], round & 1))) { *aborted = 1; break; }
+        if (!warp_wait(&full[s], round & 1)) { *aborted = 1; break; }
         const uint8_t* rowp = base + size_t(s) * L.stage_bytes + row * 128;
 #pragma unroll
         for (int p = 0; p < 8; ++p) {

@@ -254,7 +254,7 @@ tc2_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant
       for (int it = 0; it < iters; ++it) {
         const int s = it % stages, round = it / stages;
         // The MMAs that read slot s are done, so its X tile has landed and stays until we release it.
-        if (!__all_sync(0xffffffffu, mbar_wait(&mdone[s], round & 1))) { *aborted = 1; break; }
+        if (!warp_wait(&mdone[s], round & 1)) { *aborted = 1; break; }
         const uint8_t* rowp = base + size_t(s) * L.stage_bytes + row * 128;
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
