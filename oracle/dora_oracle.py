@@ -3,8 +3,8 @@
 This module restates, in numpy, what the reference (sockeye44/dorafactors, a
 patched HuggingFace PEFT) computes on its eager PyTorch path for the three hot
 operations: the factored row norm, the compose forward and the compose
-backward.  It is the checker for the CUDA kernels and the timed CPU baseline in
-``bench.py --impl reference``; nothing in the product package imports it.
+backward.  The tests compare the CUDA kernels against it, and ``bench.py`` times it
+as the CPU baseline (``--impl reference``); nothing in the product package imports it.
 
 Numerics model.  Arrays are float32 numpy arrays whose values are exactly
 representable in the logical dtype (``"bf16"``, ``"fp16"`` or ``"fp32"``).  Each
