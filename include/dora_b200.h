@@ -39,7 +39,7 @@ typedef enum {
 typedef enum {
   DORA_OK = 0,
   DORA_ERR_INVALID_ARGUMENT = 1, /* bad size, dtype, null pointer or alias */
-  DORA_ERR_UNSUPPORTED = 2,      /* valid request this build cannot serve */
+  DORA_ERR_UNSUPPORTED = 2,      /* valid request this library cannot serve */
   DORA_ERR_WORKSPACE = 3,        /* workspace missing or too small */
   DORA_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed */
   DORA_ERR_DEVICE_TIMEOUT = 5    /* a bounded device-side wait gave up */
