@@ -47,6 +47,7 @@ __host__ __device__ inline int64_t sk_owner(int64_t x, int64_t total, int64_t gr
 struct SkArgs {
   int64_t M, N;
   int nt, ybox, m_tiles, n_tiles, kblocks, stages, grid, slots;
+  int ksub;            // 64-deep k-blocks per unit (one ring stage); kblocks counts units
   int apart;           // Z and the G slots have their own region after the ring (else they reuse the ring)
   uint32_t stage_off;  // Z / G region, from the 1024-aligned base
   uint32_t bar_off;    // barriers, from the 1024-aligned base
@@ -64,17 +65,17 @@ __host__ __device__ inline uint32_t sk_stage_bytes(int nt) { return kXTileBytes 
 // narrow enough) a separate region for the staged Z rows and two G slots, so
 // the next segment's ring loads can stream in while this segment's epilogue
 // runs; wide tiles stage Z / G in the idle ring instead.
-// Narrow tiles (small r) stream W0 with up to 12 stages in flight: at r = 16 a stage
-// is 18 KB, and more bytes in flight per SM is what the HBM stream needs.
+// At most 12 stages; narrow tiles fill the ring with fewer, deeper stages instead
+// (sk_layout below).
 constexpr int kMaxSkStages = 12;
 
 struct SkLayout {
-  int stages, apart;
+  int stages, apart, ksub;
   uint32_t stage_off, bar_off, total;
 };
-inline SkLayout sk_layout(int nt, bool fuse_v) {
+inline SkLayout sk_layout_k(int nt, bool fuse_v, int ksub) {
   const uint32_t budget = 220u * 1024u;
-  const uint32_t stage = sk_stage_bytes(nt);
+  const uint32_t stage = sk_stage_bytes(nt) * uint32_t(ksub);
   const uint32_t z_bytes = uint32_t((nt + BK - 1) / BK) * kXTileBytes;
   const uint32_t staging = z_bytes + (fuse_v ? 2u * uint32_t(nt) * 128u : 0u);
   SkLayout L{};
@@ -93,7 +94,21 @@ inline SkLayout sk_layout(int nt, bool fuse_v) {
     L.bar_off = stage * uint32_t(L.stages);
   }
   L.total = 1024u + L.bar_off + 512u;  // barriers (2 per stage + 10) and two words
+  L.ksub = ksub;
   return L;
+}
+
+// Units (ring stages) of up to four 64-deep k-blocks, as many as keep three stages in
+// flight.  Every unit pays a fixed hand-off (TMA issue, MMA issue and commit, the row
+// sums' release), which narrow tiles do not hide behind their few bytes per k-block:
+// at 28672 x 8192 bf16, r = 16 went from 0.169 to 0.140 ms with four k-blocks per unit,
+// r = 128 from 0.183 to 0.161 ms with two.  Wide tiles keep one k-block per unit.
+inline SkLayout sk_layout(int nt, bool fuse_v) {
+  for (int k = 4; k > 1; --k) {
+    const SkLayout L = sk_layout_k(nt, fuse_v, k);
+    if (L.stages >= 3) return L;
+  }
+  return sk_layout_k(nt, fuse_v, 1);
 }
 
 template <typename T, bool kSumSq>
@@ -104,7 +119,9 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int nt = a.nt, S = a.stages;
-  const uint32_t stage_bytes = sk_stage_bytes(nt);
+  const uint32_t sub_bytes = sk_stage_bytes(nt);  // one 64-deep k-block of X and Y
+  const int ksub = a.ksub;
+  const uint32_t stage_bytes = sub_bytes * uint32_t(ksub);
   uint8_t* zbase = base + a.stage_off;  // staged Z rows, then two G slots
   uint64_t* full = reinterpret_cast<uint64_t*>(base + a.bar_off);
   uint64_t* empty = full + S;
@@ -203,12 +220,16 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
           const int s = int(g % S);
           if (g >= S && !mbar_wait(&empty[s], uint32_t((g / S - 1) & 1))) { *aborted = 1; break; }
           if (*aborted) break;
-          const int kx = (sg.ua + i) * BK;
-          uint8_t* sX = base + size_t(s) * stage_bytes;
+          uint8_t* stage = base + size_t(s) * stage_bytes;
+          // The last unit's k-blocks past K read the fill value (zero) and count in full.
           mbar_expect_tx(&full[s], stage_bytes);
-          tma_load_2d(sX, &tmX, &full[s], kx, m0);
-          for (int j = 0; j * a.ybox < nt; ++j)
-            tma_load_2d(sX + kXTileBytes + size_t(j) * a.ybox * 128, &tmY, &full[s], kx, n0 + j * a.ybox);
+          for (int h = 0; h < ksub; ++h) {
+            const int kx = ((sg.ua + i) * ksub + h) * BK;
+            uint8_t* sX = stage + size_t(h) * sub_bytes;
+            tma_load_2d(sX, &tmX, &full[s], kx, m0);
+            for (int j = 0; j * a.ybox < nt; ++j)
+              tma_load_2d(sX + kXTileBytes + size_t(j) * a.ybox * 128, &tmY, &full[s], kx, n0 + j * a.ybox);
+          }
           ++gk;
           // Start the tile's Z rows towards L2 a few k-blocks before they are staged.
           if (i == (sg.u_iters > S + 1 ? sg.u_iters - S - 1 : 0))
@@ -268,8 +289,11 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
           const int s = int(g % S);
           if (!mbar_wait(&full[s], uint32_t((g / S) & 1))) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sX = smem_u32(base + size_t(s) * stage_bytes);
-          mma_kblock(tmem_base, sX, sX + kXTileBytes, chunks, i > 0);
+          const uint32_t stage = smem_u32(base + size_t(s) * stage_bytes);
+          for (int h = 0; h < ksub; ++h) {
+            const uint32_t sX = stage + uint32_t(h) * sub_bytes;
+            mma_kblock(tmem_base, sX, sX + kXTileBytes, chunks, i > 0 || h > 0);
+          }
           umma_commit(&empty[s]);
         }
         if (!ok) break;
@@ -348,16 +372,18 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
             if (lane == 0) mbar_arrive(&empty[s]);
             continue;
           }
-          const uint8_t* rowp = base + size_t(s) * stage_bytes + row * 128;
+          for (int hb = 0; hb < ksub; ++hb) {
+            const uint8_t* rowp = base + size_t(s) * stage_bytes + size_t(hb) * sub_bytes + row * 128;
 #pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            // Rotate the 16-byte chunk order by lane so a quarter-warp touches 8 distinct bank groups.
-            const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((p + lane) & 7) * 16);
-            const T* h = reinterpret_cast<const T*>(&v);
+            for (int p = 0; p < 8; ++p) {
+              // Rotate the 16-byte chunk order by lane so a quarter-warp touches 8 distinct bank groups.
+              const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((p + lane) & 7) * 16);
+              const T* h = reinterpret_cast<const T*>(&v);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float x = to_f32(h[e]);
-              ssq8[e] = fmaf(x, x, ssq8[e]);
+              for (int e = 0; e < 8; ++e) {
+                const float x = to_f32(h[e]);
+                ssq8[e] = fmaf(x, x, ssq8[e]);
+              }
             }
           }
           __syncwarp();
@@ -440,7 +466,8 @@ bool tc_sk_supported(const TcGemmArgs& a) {
 SkPlan tc_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
   const TcGemmShape sh = tc_gemm_shape(M, N, K);
   SkPlan p;
-  p.units_per_tile = int64_t(sh.kblocks) + (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
+  const int ksub = tc::sk_layout(sh.nt, fuse_v).ksub;
+  p.units_per_tile = int64_t((sh.kblocks + ksub - 1) / ksub) + (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
   const int64_t tiles = int64_t(sh.m_tiles) * sh.n_tiles;
   p.total_units = tiles * p.units_per_tile;
   // One CTA per SM, but no CTA with fewer than four units (each segment pays a staging and epilogue).
@@ -500,8 +527,9 @@ int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.ybox = ybox;
   k.m_tiles = sh.m_tiles;
   k.n_tiles = sh.n_tiles;
-  k.kblocks = sh.kblocks;
   const tc::SkLayout L = tc::sk_layout(sh.nt, fuse);
+  k.ksub = L.ksub;
+  k.kblocks = (sh.kblocks + L.ksub - 1) / L.ksub;  // units of ksub k-blocks
   k.stages = L.stages;
   k.apart = L.apart;
   k.stage_off = L.stage_off;
@@ -510,7 +538,7 @@ int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.slots = p.slots;
   k.fuse_v = fuse ? 1 : 0;
   k.v_kblocks = int((a.N + tc::BK - 1) / tc::BK);
-  k.units_per_tile = int64_t(sh.kblocks) + (fuse ? 2 * k.v_kblocks : 0);
+  k.units_per_tile = int64_t(k.kblocks) + (fuse ? 2 * k.v_kblocks : 0);
   k.total_units = int64_t(sh.m_tiles) * sh.n_tiles * k.units_per_tile;
   if (k.units_per_tile != p.units_per_tile || k.total_units != p.total_units) return DORA_ERR_INVALID_ARGUMENT;
   uint32_t cols = 32;
