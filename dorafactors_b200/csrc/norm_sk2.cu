@@ -38,6 +38,7 @@ __host__ __device__ inline int64_t sk2_owner(int64_t x, int64_t total, int64_t g
 struct Sk2Args {
   int64_t M, N;
   int nt, pair_tiles, kblocks, stages, clusters, slots;
+  int ksub;  // 64-deep k-blocks per unit (one ring stage); kblocks counts units
   int apart;
   uint32_t stage_off, bar_off;
   int fuse_v, v_kblocks;
@@ -51,12 +52,12 @@ struct Sk2Args {
 __host__ __device__ inline uint32_t sk2_stage_bytes(int nt) { return kXTileBytes + uint32_t(nt) * 64u; }
 
 struct Sk2Layout {
-  int stages, apart;
+  int stages, apart, ksub;
   uint32_t stage_off, bar_off, total;
 };
-inline Sk2Layout sk2_layout(int nt, bool fuse_v) {
+inline Sk2Layout sk2_layout_k(int nt, bool fuse_v, int ksub) {
   const uint32_t budget = 220u * 1024u;
-  const uint32_t stage = sk2_stage_bytes(nt);
+  const uint32_t stage = sk2_stage_bytes(nt) * uint32_t(ksub);
   const uint32_t z_bytes = uint32_t((nt + BK - 1) / BK) * kXTileBytes;
   const uint32_t staging = z_bytes + (fuse_v ? 2u * uint32_t(nt) * 64u : 0u);
   Sk2Layout L{};
@@ -75,7 +76,16 @@ inline Sk2Layout sk2_layout(int nt, bool fuse_v) {
     L.bar_off = stage * uint32_t(L.stages);
   }
   L.total = 1024u + L.bar_off + 512u;
+  L.ksub = ksub;
   return L;
+}
+// As in the single-CTA kernel: units of up to four k-blocks while three stages fit.
+inline Sk2Layout sk2_layout(int nt, bool fuse_v) {
+  for (int k = 4; k > 1; --k) {
+    const Sk2Layout L = sk2_layout_k(nt, fuse_v, k);
+    if (L.stages >= 3) return L;
+  }
+  return sk2_layout_k(nt, fuse_v, 1);
 }
 
 template <typename T>
@@ -86,7 +96,9 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int nt = a.nt, S = a.stages;
-  const uint32_t stage_bytes = sk2_stage_bytes(nt);
+  const uint32_t sub_bytes = sk2_stage_bytes(nt);  // one 64-deep k-block of X and this CTA's Y half
+  const int ksub = a.ksub;
+  const uint32_t stage_bytes = sub_bytes * uint32_t(ksub);
   uint8_t* zbase = base + a.stage_off;
   uint64_t* full = reinterpret_cast<uint64_t*>(base + a.bar_off);  // leader: both halves of a stage landed
   uint64_t* mdone = full + S;       // both: the MMA finished reading the stage
@@ -188,12 +200,15 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
           const int s = int(g % S);
           if (g >= S && !slot_free(g - S)) { *aborted = 1; break; }
           if (*aborted) break;
-          const int kx = (sg.ua + i) * BK;
-          uint8_t* sX = base + size_t(s) * stage_bytes;
+          uint8_t* stage = base + size_t(s) * stage_bytes;
           const uint32_t bar_c = map_to_rank(&full[s], 0);
           if (leader) mbar_expect_tx(&full[s], 2u * stage_bytes);
-          tma_load_2d_pair(sX, &tmX, bar_c, kx, m0);
-          tma_load_2d_pair(sX + kXTileBytes, &tmY, bar_c, kx, int(rank) * half_rows);
+          for (int h = 0; h < ksub; ++h) {  // k-blocks past K read zeros and count in full
+            const int kx = ((sg.ua + i) * ksub + h) * BK;
+            uint8_t* sX = stage + size_t(h) * sub_bytes;
+            tma_load_2d_pair(sX, &tmX, bar_c, kx, m0);
+            tma_load_2d_pair(sX + kXTileBytes, &tmY, bar_c, kx, int(rank) * half_rows);
+          }
           ++gk;
           if (i == (sg.u_iters > S + 1 ? sg.u_iters - S - 1 : 0))
             for (int j = 0; j < nzb; ++j) tma_prefetch_2d(&tmZ, j * BK, m0);
@@ -250,8 +265,11 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
           const int s = int(g % S);
           if (!mbar_wait(&full[s], uint32_t((g / S) & 1))) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sX = smem_u32(base + size_t(s) * stage_bytes);
-          mma2_kblock(tmem_base, sX, sX + kXTileBytes, chunks, i > 0);
+          const uint32_t stage = smem_u32(base + size_t(s) * stage_bytes);
+          for (int h = 0; h < ksub; ++h) {
+            const uint32_t sX = stage + uint32_t(h) * sub_bytes;
+            mma2_kblock(tmem_base, sX, sX + kXTileBytes, chunks, i > 0 || h > 0);
+          }
           umma2_commit_both(&mdone[s]);
         }
         if (!ok) break;
@@ -325,15 +343,17 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
         const int64_t g = gk++;
         const int s = int(g % S);
         if (!warp_wait(&mdone[s], uint32_t((g / S) & 1))) { ok = false; break; }
-        const uint8_t* rowp = base + size_t(s) * stage_bytes + row * 128;
+        for (int hb = 0; hb < ksub; ++hb) {
+          const uint8_t* rowp = base + size_t(s) * stage_bytes + size_t(hb) * sub_bytes + row * 128;
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((p + lane) & 7) * 16);
-          const T* h = reinterpret_cast<const T*>(&v);
+          for (int p = 0; p < 8; ++p) {
+            const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((p + lane) & 7) * 16);
+            const T* h = reinterpret_cast<const T*>(&v);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float x = to_f32(h[e]);
-            ssq8[e] = fmaf(x, x, ssq8[e]);
+            for (int e = 0; e < 8; ++e) {
+              const float x = to_f32(h[e]);
+              ssq8[e] = fmaf(x, x, ssq8[e]);
+            }
           }
         }
         __syncwarp();
@@ -422,7 +442,8 @@ SkPlan tc2_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
   const TcGemmShape sh = tc_gemm_shape(M, N, K);
   SkPlan p;
   const int64_t pair_tiles = (M + 2 * tc::BM - 1) / (2 * tc::BM);
-  p.units_per_tile = int64_t(sh.kblocks) + (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
+  const int ksub = tc::sk2_layout(sh.nt, fuse_v).ksub;
+  p.units_per_tile = int64_t((sh.kblocks + ksub - 1) / ksub) + (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
   p.total_units = pair_tiles * p.units_per_tile;
   int64_t g = p.total_units / 4;
   if (g > sms / 2) g = sms / 2;
@@ -477,7 +498,8 @@ int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.N = a.N;
   k.nt = sh.nt;
   k.pair_tiles = int((a.M + 2 * tc::BM - 1) / (2 * tc::BM));
-  k.kblocks = sh.kblocks;
+  k.ksub = L.ksub;
+  k.kblocks = (sh.kblocks + L.ksub - 1) / L.ksub;  // units of ksub k-blocks
   k.stages = L.stages;
   k.clusters = p.grid;
   k.slots = p.slots;
@@ -486,7 +508,7 @@ int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.bar_off = L.bar_off;
   k.fuse_v = fuse ? 1 : 0;
   k.v_kblocks = int((a.N + tc::BK - 1) / tc::BK);
-  k.units_per_tile = int64_t(sh.kblocks) + (fuse ? 2 * k.v_kblocks : 0);
+  k.units_per_tile = int64_t(k.kblocks) + (fuse ? 2 * k.v_kblocks : 0);
   k.total_units = int64_t(k.pair_tiles) * k.units_per_tile;
   if (k.units_per_tile != p.units_per_tile || k.total_units != p.total_units) return DORA_ERR_INVALID_ARGUMENT;
   uint32_t cols = 32;
