@@ -102,11 +102,16 @@ inline SkLayout sk_layout_k(int nt, bool fuse_v, int ksub) {
 // flight.  Every unit pays a fixed hand-off (TMA issue, MMA issue and commit, the row
 // sums' release), which narrow tiles do not hide behind their few bytes per k-block:
 // at 28672 x 8192 bf16, r = 16 went from 0.169 to 0.140 ms with four k-blocks per unit,
-// r = 128 from 0.183 to 0.161 ms with two.  Wide tiles keep one k-block per unit.
+// r = 128 from 0.183 to 0.161 ms with two.  Below 256 columns two k-blocks per unit pay
+// even with only two stages (r = 192: 0.202 -> 0.184 ms); wider tiles keep one.
 inline SkLayout sk_layout(int nt, bool fuse_v) {
   for (int k = 4; k > 1; --k) {
     const SkLayout L = sk_layout_k(nt, fuse_v, k);
     if (L.stages >= 3) return L;
+  }
+  if (nt < 256) {
+    const SkLayout L = sk_layout_k(nt, fuse_v, 2);
+    if (L.stages >= 2) return L;
   }
   return sk_layout_k(nt, fuse_v, 1);
 }
