@@ -151,7 +151,16 @@ __global__ void gram_reduce_kernel(const float* __restrict__ part, int nsplit, i
 #pragma unroll
         for (int q = 0; q < 8; ++q) v += t[q];
       }
-      for (; z < nsplit; ++z) v += p[int64_t(z) * rr];
+      if (z < nsplit) {
+        // The last (or only) batch also keeps its loads in flight together: at r = 1024
+        // (four splits) a one-by-one tail made this kernel 27 us instead of a few.
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = (z + q < nsplit) ? p[int64_t(z + q) * rr] : 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (z + q < nsplit) v += t[q];
+      }
     }
     tile[yy][tx] = v;
   }
