@@ -50,6 +50,8 @@ struct Sk2Args {
 };
 
 __host__ __device__ inline uint32_t sk2_stage_bytes(int nt) { return kXTileBytes + uint32_t(nt) * 64u; }
+// G k-block slots of the fused B G B^T phase (a ring of its own, staged after Z).
+constexpr int kVSlots = 4;
 
 struct Sk2Layout {
   int stages, apart, ksub;
@@ -59,7 +61,7 @@ inline Sk2Layout sk2_layout_k(int nt, bool fuse_v, int ksub) {
   const uint32_t budget = 220u * 1024u;
   const uint32_t stage = sk2_stage_bytes(nt) * uint32_t(ksub);
   const uint32_t z_bytes = uint32_t((nt + BK - 1) / BK) * kXTileBytes;
-  const uint32_t staging = z_bytes + (fuse_v ? 2u * uint32_t(nt) * 64u : 0u);
+  const uint32_t staging = z_bytes + (fuse_v ? uint32_t(kVSlots) * uint32_t(nt) * 64u : 0u);
   Sk2Layout L{};
   int s_apart = staging < budget ? int((budget - staging) / stage) : 0;
   if (s_apart > 8) s_apart = 8;
@@ -106,9 +108,9 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
   uint64_t* done = empty + S;       // both: the segment's X Y^T units are accumulated
   uint64_t* zfull = done + 1;       // local: this CTA's Z rows are staged
   uint64_t* peer_z = zfull + 1;     // leader: the peer's Z rows are staged
-  uint64_t* vfull = peer_z + 1;     // [2] leader: both halves of a G k-block landed
-  uint64_t* vempty = vfull + 2;     // [2] both: the MMA finished reading a G slot
-  uint64_t* tmem_free = vempty + 2; // leader: all rows of the pair finished the first epilogue
+  uint64_t* vfull = peer_z + 1;            // [kVSlots] leader: both halves of a G k-block landed
+  uint64_t* vempty = vfull + kVSlots;      // [kVSlots] both: the MMA finished reading a G slot
+  uint64_t* tmem_free = vempty + kVSlots;  // leader: all rows of the pair finished the first epilogue
   uint64_t* vdone = tmem_free + 1;  // both: the segment's Z G^T units are accumulated
   uint64_t* seg_free = vdone + 1;   // local: this CTA's rows are done with staged Z / G
   uint64_t* tm_free = seg_free + 1; // leader: all rows of the pair are done with TMEM
@@ -137,7 +139,7 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
     mbar_init(done, 1);
     mbar_init(zfull, 1);
     mbar_init(peer_z, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kVSlots; ++s) {
       mbar_init(&vfull[s], 1);
       mbar_init(&vempty[s], 1);
     }
@@ -230,8 +232,8 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
         for (int i = 0; i < sg.v_iters; ++i) {
           if (gv == 0) pdl_wait();  // G (hi / lo) is written by the previous kernel
           const int64_t g = gv;
-          const int vs = int(g & 1);
-          if (g >= 2 && !mbar_wait(&vempty[vs], uint32_t((g / 2 - 1) & 1))) { *aborted = 1; break; }
+          const int vs = int(g % kVSlots);
+          if (g >= kVSlots && !mbar_wait(&vempty[vs], uint32_t((g / kVSlots - 1) & 1))) { *aborted = 1; break; }
           const int kv = sg.v0 + i;
           const bool lo = kv >= vkb;
           const int kx = (lo ? kv - vkb : kv) * BK;
@@ -244,7 +246,8 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
       }
       // Keep this thread until the MMAs have consumed what it loaded (bounded waits).
       for (int64_t g = gk - S > 0 ? gk - S : 0; g < gk; ++g) mbar_wait(&mdone[g % S], uint32_t((g / S) & 1));
-      for (int64_t g = gv - 2 > 0 ? gv - 2 : 0; g < gv; ++g) mbar_wait(&vempty[g & 1], uint32_t((g / 2) & 1));
+      for (int64_t g = gv - kVSlots > 0 ? gv - kVSlots : 0; g < gv; ++g)
+        mbar_wait(&vempty[g % kVSlots], uint32_t((g / kVSlots) & 1));
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
@@ -283,8 +286,8 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
           tc_fence_after();
           for (int i = 0; i < sg.v_iters; ++i) {
             const int64_t g = gv++;
-            const int vs = int(g & 1);
-            if (!mbar_wait(&vfull[vs], uint32_t((g / 2) & 1))) { ok = false; break; }
+            const int vs = int(g % kVSlots);
+            if (!mbar_wait(&vfull[vs], uint32_t((g / kVSlots) & 1))) { ok = false; break; }
             tc_fence_after();
             const int kv = sg.v0 + i;
             const int kz = kv >= vkb ? kv - vkb : kv;
@@ -432,7 +435,7 @@ bool tc2_sk_supported(const TcGemmArgs& a) {
   if (sh.n_tiles != 1 || a.M < 2 * tc::BM) return false;
   const tc::Sk2Layout L = tc::sk2_layout(sh.nt, a.G1 != nullptr);
   const uint32_t z_bytes = uint32_t((sh.nt + tc::BK - 1) / tc::BK) * tc::kXTileBytes;
-  const uint32_t staging = z_bytes + (a.G1 ? 2u * uint32_t(sh.nt) * 64u : 0u);
+  const uint32_t staging = z_bytes + (a.G1 ? uint32_t(tc::kVSlots) * uint32_t(sh.nt) * 64u : 0u);
   if (L.stages < 2 || (!L.apart && staging > L.bar_off)) return false;
   if (a.G1 && (!a.G2 || !a.v_part || !tc_can_fuse_v(a.M, a.N, a.K))) return false;
   return true;
