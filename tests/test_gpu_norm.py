@@ -90,6 +90,7 @@ CASES = [
     (300, 512, 600, "bf16"),  # three N tiles of the row-dot GEMM, the last one ragged
     (700, 2048, 200, "bf16"),  # two k-blocks per stream-K stage, two stages
     (300, 1000, 176, "fp16"),  # the same with a ragged last unit (16 k-blocks, K % 64 != 0)
+    (700, 4160, 256, "bf16"),  # CTA-pair stream-K, two k-blocks per stage, 65 k-blocks (last stage half past K)
 ]
 
 
@@ -183,7 +184,7 @@ from dorafactors_b200 import _native
 out = {}
 for out_f, in_f, r in ((28672, 8192, 384), (8192, 4096, 256), (1000, 2048, 384), (640, 1024, 64),
                       (8192, 8192, 16), (4096, 4096, 512), (257, 320, 40), (2048, 2048, 768), (640, 1024, 520),
-                      (3000, 4104, 200)):
+                      (3000, 4104, 200), (1500, 4160, 256)):
     g = torch.Generator(device="cuda").manual_seed(out_f + r)
     W = (torch.randn(out_f, in_f, device="cuda", generator=g) * 0.02).bfloat16()
     A = ((torch.rand(r, in_f, device="cuda", generator=g) * 2 - 1) / in_f**0.5).bfloat16()
