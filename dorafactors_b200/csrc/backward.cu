@@ -303,7 +303,9 @@ static void* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of g_bwd_scratch on the current device.  In host code the
 // symbol's name is only a host-side stand-in, so the address is looked up once
-// per device (with that device current) and cached.
+// per device (with that device current) and cached.  The cache is never
+// invalidated: after cudaDeviceReset the cached address belongs to the old
+// context, so this entry point must not be used across a device reset.
 static int static_scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -326,6 +328,7 @@ extern "C" int dora_compose_bwd_noalloc(const void* d_out, const void* inner, co
                                         double scale, void* d_lora, void* d_base, void* d_g, int64_t rows,
                                         int64_t cols, int act_dtype, void* stream) {
   if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
+  if (g_dtype != act_dtype && g_dtype != DORA_DTYPE_F32) return DORA_ERR_INVALID_ARGUMENT;
   if (!d_g || rows == 0 || cols == 0) {
     // No column sum (or nothing to sum over): no scratch is touched.
     return dora_compose_bwd(d_out, inner, g, g_dtype, scale, d_lora, d_base, d_g, nullptr, 0, rows, cols,
@@ -333,6 +336,9 @@ extern "C" int dora_compose_bwd_noalloc(const void* d_out, const void* inner, co
   }
   const size_t need = dora_compose_bwd_workspace_size(rows, cols, act_dtype);
   if (need > kStaticScratchBytes) return DORA_ERR_WORKSPACE;
+  // The rest of dora_compose_bwd's argument checks run before the array is
+  // touched, so a call that will be rejected queues nothing on it.
+  if (!inner || !d_out || !g) return DORA_ERR_INVALID_ARGUMENT;
   void* ws = nullptr;
   int rc = static_scratch_address(&ws);
   if (rc != DORA_OK) return rc;

@@ -199,6 +199,9 @@ int dora_compose_bwd_channels(const void* d_out, const void* inner, const void* 
  * made.  The scratch is a fixed DORA_NOALLOC_SCRATCH_BYTES array inside the
  * library's device image; a shape whose dora_compose_bwd_workspace_size()
  * exceeds it is rejected with DORA_ERR_WORKSPACE before anything is queued.
+ * That size depends on the current device's SM count (the backward's grid),
+ * so the largest accepted shape does too.  Argument errors are reported
+ * before the array is touched.
  *
  * The first call on each device looks up the array's device address (with
  * that device current) and caches it; make that first call before any stream
@@ -207,7 +210,8 @@ int dora_compose_bwd_channels(const void* d_out, const void* inner, const void* 
  * stream first.  Calls that overlap on the GPU (different streams, or
  * different host threads without ordering) race on the array and give wrong
  * d_g; order them on one stream or use dora_compose_bwd with separate
- * workspaces instead.
+ * workspaces instead.  The cached address does not survive cudaDeviceReset:
+ * do not call this entry point on a device after resetting it.
  */
 int dora_compose_bwd_noalloc(const void* d_out, const void* inner, const void* g, int g_dtype, double scale,
                              void* d_lora, void* d_base, void* d_g, int64_t rows, int64_t cols, int act_dtype,

@@ -27,15 +27,30 @@ def _lib():
 
 def test_noalloc_rejects_oversized_shapes_before_any_work():
     """A shape whose scratch need exceeds the fixed array fails with DORA_ERR_WORKSPACE.
-    The size check runs on the host before any CUDA call, so no GPU is needed."""
+
+    The size check is host arithmetic (it reads the current device's SM count,
+    148 when no device is visible) and runs before the array is touched, so no
+    GPU is needed.  The activation pointers are null: should the size check
+    ever let the shape through, the null-pointer check still rejects the call
+    before anything is queued, so no kernel can run on a made-up address."""
     native, lib = _lib()
     rows, cols = 4, 1 << 20
     need = lib.dora_compose_bwd_workspace_size(rows, cols, BF16)
     assert need > 4 * 2**20
-    vp = ctypes.c_void_p
-    rc = lib.dora_compose_bwd_noalloc(vp(1 << 20), vp(2 << 20), vp(3 << 20), BF16, 1.0, None, None,
-                                      vp(4 << 20), rows, cols, BF16, None)
+    d_g = ctypes.c_void_p(4 << 20)  # never dereferenced: the call is rejected on the host
+    rc = lib.dora_compose_bwd_noalloc(None, None, None, BF16, 1.0, None, None, d_g, rows, cols, BF16, None)
     assert rc == native.ERR_WORKSPACE
+
+
+def test_noalloc_rejects_null_operands_before_any_work():
+    """A shape that fits but has no inner / d_out / g is an argument error, reported
+    before the shared array is looked up or cleared (nothing is queued)."""
+    native, lib = _lib()
+    d_g = ctypes.c_void_p(4 << 20)  # never dereferenced
+    rc = lib.dora_compose_bwd_noalloc(None, None, None, BF16, 1.0, None, None, d_g, 8, 64, BF16, None)
+    assert rc == native.ERR_INVALID_ARGUMENT
+    rc = lib.dora_compose_bwd_noalloc(None, None, None, 7, 1.0, None, None, d_g, 8, 64, BF16, None)
+    assert rc == native.ERR_INVALID_ARGUMENT
 
 
 @pytest.mark.gpu
@@ -73,8 +88,11 @@ def test_noalloc_matches_workspace_entry_point_twice():
         exact = (inner.double() * d_out.double()).sum(0).cpu().numpy()
         assert_close(got[2].float().cpu().numpy(), exact, RTOL["bf16"], "noalloc d_g vs float64 sum")
 
-    # Two calls in a row, different shapes and data: the second reuses the
-    # scratch the first left behind.
+    # Calls in a row, different shapes and data: each reuses the scratch the
+    # previous one left behind.  2055 columns (not a multiple of 8) take the
+    # scalar plan, whose counter region differs from the vectorised plan's.
     run(4097, 2056, seed=1, scale=1.25)
     run(16384, 28672, seed=2, scale=1.0)
+    run(4097, 2055, seed=3, scale=0.75)
+    run(333, 2056, seed=4, scale=2.0)
     assert native.device_error(reset=True) == 0
