@@ -39,7 +39,7 @@ sys.path.insert(0, ROOT)
 OUT_F, IN_F, RANK, TOKENS, SCALE = 28672, 8192, 384, 16384, 1.0
 METRIC = "DoRA layer fwd+bwd tokens/s, norm TFLOP/s & compose HBM GB/s vs peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-CPU_SAMPLE_TOKENS = 128
+CPU_SAMPLE_TOKENS = 4096  # tokens per host-core step: a quarter of the workload's 16384
 
 
 def workload_config(parallelism: str) -> dict:
@@ -415,82 +415,156 @@ def read_traffic(kernel: str):
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline / reference arm: the oracle (numpy restatement of the eager path)
+# CPU baseline / reference arm: the reference's own eager DoRA layer on the
+# host cores (its dora.py / dora_fused.py, byte-compiled into oracle/_ref by
+# oracle/build_ref.py), or the numpy oracle when that build is absent.
 # ---------------------------------------------------------------------------
-def _cpu_inputs(tokens: int, seed: int = 0):
-    """Seeded bf16-valued inputs as float32 numpy arrays (generated with torch for speed)."""
-    import torch
-
-    g = torch.Generator().manual_seed(seed)
-
-    def bf(t):
-        return t.bfloat16().float().numpy()
-
-    W = bf(torch.randn(OUT_F, IN_F, generator=g) * 0.02)
-    A = bf((torch.rand(RANK, IN_F, generator=g) * 2 - 1) / IN_F**0.5)
-    B = bf(torch.randn(OUT_F, RANK, generator=g) * 0.01)
-    x = bf(torch.randn(tokens, IN_F, generator=g))
-    dy = bf(torch.randn(tokens, OUT_F, generator=g))
-    return W, A, B, x, dy
+def cpu_threads() -> int:
+    """Host threads this process may use (its CPU affinity, not OMP_NUM_THREADS)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - non-Linux
+        return os.cpu_count() or 1
 
 
-def cpu_step(W, A, B, x, dy, m):
-    from oracle import dora_oracle as orc
-
-    t0 = time.perf_counter()
-    orc.dora_linear_forward_backward(x, W, None, A, B, m, SCALE, dy, "bf16")
-    return time.perf_counter() - t0
-
-
-def cpu_norm(W, A, B):
-    from oracle import dora_oracle as orc
-
-    t0 = time.perf_counter()
-    n, _ = orc.weight_norm_factored(W, A, B, SCALE, "bf16")
-    return time.perf_counter() - t0, n
+def extrapolate_full_step(t_norm: float, t_step: float, tokens: int, full_tokens: int = TOKENS) -> float:
+    """Seconds of one full-workload step estimated from a step on ``tokens`` tokens
+    (``t_step``, which includes one factored norm) and the norm alone (``t_norm``):
+    the token-proportional part scales, the norm does not."""
+    return t_norm + max(t_step - t_norm, 0.0) * (full_tokens / tokens)
 
 
-def cpu_tokens_per_s(t_norm: float, t_step: float) -> float:
-    """Full-workload tokens/s extrapolated from one norm over the full weight and a
-    forward+backward on CPU_SAMPLE_TOKENS tokens (which also recomputes the norm)."""
-    t_tok = max(t_step - t_norm, 1e-9)
-    full = t_norm + t_tok * (TOKENS / CPU_SAMPLE_TOKENS)
-    return TOKENS / full
+class CpuLayerStep:
+    """One forward + backward of the adapted linear on the host cores, on ``tokens``
+    tokens of the benchmark workload (full 28672 x 8192 r=384 bf16 weight, s=1.0).
+
+    kind "reference": the reference's ``DoraLinearLayer`` (dora.py:1380-1484) on its
+    eager CPU path, wired as ``DoraLinearVariant.forward`` wires it with no bias and
+    no dropout (``y = result + delta``, variants.py:214-284), loss gradient ``dy``;
+    the norm alone is ``_get_weight_norm_linear`` (dora.py:1024-1153).
+    kind "port": the numpy oracle's restatement of the same step.
+    """
+
+    def __init__(self, tokens: int, seed: int = 0):
+        import math
+
+        import torch
+
+        self.tokens = tokens
+        self.threads = cpu_threads()
+        torch.set_num_threads(self.threads)  # torchrun exports OMP_NUM_THREADS=1
+        g = torch.Generator().manual_seed(seed)
+        W = (torch.randn(OUT_F, IN_F, generator=g) * 0.02).bfloat16()
+        A = ((torch.rand(RANK, IN_F, generator=g) * 2 - 1) / math.sqrt(IN_F)).bfloat16()
+        B = (torch.randn(OUT_F, RANK, generator=g) * 0.01).bfloat16()
+        x = torch.randn(tokens, IN_F, generator=g).bfloat16()
+        dy = torch.randn(tokens, OUT_F, generator=g).bfloat16()
+        try:
+            from oracle.build_ref import load_reference
+
+            dora, _ = load_reference()
+            self.kind = "reference"
+        except Exception as exc:  # oracle/_ref not built: fall back to the numpy port
+            self.kind = "port"
+            self.why_port = f"{type(exc).__name__}: {exc}"
+        if self.kind == "reference":
+            from torch import nn
+
+            self.base = nn.Linear(IN_F, OUT_F, bias=False, dtype=torch.bfloat16)
+            self.lora_A = nn.Linear(IN_F, RANK, bias=False, dtype=torch.bfloat16)
+            self.lora_B = nn.Linear(RANK, OUT_F, bias=False, dtype=torch.bfloat16)
+            with torch.no_grad():
+                self.base.weight.copy_(W)
+                self.lora_A.weight.copy_(A)
+                self.lora_B.weight.copy_(B)
+            self.base.weight.requires_grad_(False)
+            self.layer = dora.DoraLinearLayer(fan_in_fan_out=False)
+            self.layer.update_layer(base_layer=self.base, lora_A=self.lora_A.weight, lora_B=self.lora_B.weight,
+                                    scaling=SCALE)
+            self.x = x.requires_grad_(True)
+            self.dy = dy
+        else:
+            from oracle import dora_oracle as orc
+
+            self.orc = orc
+            self.np = [t.float().numpy() for t in (W, A, B, x, dy)]
+            self.m, _ = orc.weight_norm_factored(self.np[0], self.np[1], self.np[2], SCALE, "bf16")
+
+    def step(self) -> float:
+        t0 = time.perf_counter()
+        if self.kind == "reference":
+            for p in (self.lora_A.weight, self.lora_B.weight, self.layer.weight):
+                p.grad = None
+            self.x.grad = None
+            result = self.base(self.x)
+            delta = self.layer(self.x, lora_A=self.lora_A, lora_B=self.lora_B, scaling=SCALE,
+                               base_layer=self.base, base_result=result)
+            y = result + delta
+            y.backward(self.dy)
+        else:
+            W, A, B, x, dy = self.np
+            self.orc.dora_linear_forward_backward(x, W, None, A, B, self.m, SCALE, dy, "bf16")
+        return time.perf_counter() - t0
+
+    def norm(self) -> float:
+        t0 = time.perf_counter()
+        if self.kind == "reference":
+            import torch
+
+            with torch.no_grad():
+                self.layer._get_weight_norm_linear(base_weight=self.base.weight, lora_A_w=self.lora_A.weight,
+                                                   lora_B_w=self.lora_B.weight, scaling=SCALE)
+        else:
+            W, A, B = self.np[:3]
+            self.orc.weight_norm_factored(W, A, B, SCALE, "bf16")
+        return time.perf_counter() - t0
+
+    def describe(self) -> str:
+        who = ("the reference's DoraLinearLayer (dora.py / dora_fused.py byte-compiled into oracle/_ref), "
+               "eager CPU path" if self.kind == "reference"
+               else f"numpy oracle of the reference's eager path (oracle/_ref unavailable: {self.why_port})")
+        return (f"{who}; each step: y = base(x) + DoRA delta and y.backward(dy) on {self.tokens} of the "
+                f"{TOKENS} tokens over the full {OUT_F}x{IN_F} r={RANK} bf16 weight (the factored norm is "
+                f"recomputed every step, as in training); {self.threads} host threads")
 
 
-def cpu_baseline_sample() -> dict:
-    W, A, B, x, dy = _cpu_inputs(CPU_SAMPLE_TOKENS)
-    t_norm, m = cpu_norm(W, A, B)
-    t_step = cpu_step(W, A, B, x, dy, m)
+def cpu_baseline_sample(steps: int = 3) -> dict:
+    """The CPU baseline of the native line: a few measured steps (about 10 s of host work)."""
+    c = CpuLayerStep(CPU_SAMPLE_TOKENS)
+    c.step()  # warm-up
+    t = [c.step() for _ in range(steps)]
+    t_step = sum(t) / len(t)
+    t_norm = c.norm()
+    full = extrapolate_full_step(t_norm, t_step, CPU_SAMPLE_TOKENS)
     return {
-        "value": cpu_tokens_per_s(t_norm, t_step),
+        "value": CPU_SAMPLE_TOKENS / t_step,
         "unit": "tokens/s",
-        "cores": os.cpu_count(),
-        "kind": "port",
-        "sample": (f"numpy oracle of the reference eager path: factored norm over the full "
-                   f"{OUT_F}x{IN_F} r={RANK} weight ({t_norm:.2f} s) + one forward/backward on "
-                   f"{CPU_SAMPLE_TOKENS} tokens ({t_step:.2f} s incl. its norm), extrapolated to "
-                   f"{TOKENS} tokens"),
+        "cores": c.threads,
+        "kind": c.kind,
+        "sample": c.describe() + f"; mean of {steps} steps after one warm-up",
+        "ms_per_sample_step": t_step * 1e3,
+        "extrapolated_full_workload": {"tokens_per_s": TOKENS / full, "ms_per_step": full * 1e3,
+                                       "norm_ms": t_norm * 1e3,
+                                       "how": f"norm once + token part x {TOKENS}/{CPU_SAMPLE_TOKENS}"},
     }
 
 
 def run_reference(args) -> None:
+    """The reference arm: the reference's own CPU implementation of the path, timed on
+    the host cores with all the threads this process may use.  Rank 0 only; under
+    torchrun the other ranks exit without work."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    W, A, B, x, dy = _cpu_inputs(CPU_SAMPLE_TOKENS)
-    _, m = cpu_norm(W, A, B)
+    c = CpuLayerStep(CPU_SAMPLE_TOKENS)
     for _ in range(args.warmup):
-        cpu_step(W, A, B, x, dy, m)
-    norms, steps = [], []
-    for _ in range(args.steps):
-        tn, _ = cpu_norm(W, A, B)
-        norms.append(tn)
-        steps.append(cpu_step(W, A, B, x, dy, m))
-    t_norm, t_step = statistics.median(norms), statistics.median(steps)
-    value = cpu_tokens_per_s(t_norm, t_step)
-    ms = TOKENS / value * 1e3
+        c.step()
+    times = [c.step() for _ in range(args.steps)]
+    t_step = sum(times) / len(times)
+    t_norm = c.norm()
+    full = extrapolate_full_step(t_norm, t_step, CPU_SAMPLE_TOKENS)
+    value = CPU_SAMPLE_TOKENS / t_step
     line = {
         "metric": METRIC,
         "value": value,
@@ -498,18 +572,22 @@ def run_reference(args) -> None:
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": ms,
+        "ms_per_step": t_step * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded normal / uniform weights, normal tokens)",
-        "config": workload_config("single"),
+        "config": {**workload_config("single"), "tokens_per_step_sampled": CPU_SAMPLE_TOKENS},
         "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": (f"each step: numpy oracle norm over the full weight + forward/backward on "
-                                    f"{CPU_SAMPLE_TOKENS} tokens, extrapolated to {TOKENS} tokens")},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": c.threads, "kind": c.kind,
+                         "sample": c.describe()},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "step_ms": {"median": statistics.median(times) * 1e3, "min": min(times) * 1e3, "max": max(times) * 1e3},
+        "extrapolated_full_workload": {"tokens_per_s": TOKENS / full, "ms_per_step": full * 1e3,
+                                       "norm_ms": t_norm * 1e3,
+                                       "how": (f"estimate, not a measurement: the norm once + the measured "
+                                               f"token part x {TOKENS}/{CPU_SAMPLE_TOKENS}")},
     }
     print(json.dumps(line), flush=True)
 

@@ -276,6 +276,43 @@ def dora_linear_forward_backward(x, W, bias, A, B, m, scale: float, dy, dtype: s
     return {"y": y, "delta": delta, "norm": norm, "g": g, "dx": dx, "dA": dA, "dB": dB, "dm": dm}
 
 
+def dora_linear_dropout_forward_backward(x, keep_scale, W, bias, A, B, m, scale: float, dy, dtype: str):
+    """Forward and backward of one DoRA linear with LoRA dropout active (training).
+
+    ``keep_scale`` is the dropout's fixed multiplier per input element (0 where
+    dropped, 1/(1-p) where kept), so ``xd = x * keep_scale``.  Follows
+    ``DoraLinearVariant.forward`` with a dropout (variants.py:228-232: the delta
+    is computed from ``xd`` with ``base_result=None``) and the
+    ``_compose_with_base_chunks`` branch of ``DoraLinearLayer.forward``
+    (dora.py:1470-1484, 1155-1263): the base output inside the delta is
+    recomputed as ``xd W^T`` without bias and composed eagerly
+    (``_compose_eager_inplace``, dora.py:961-1002); ``y = (x W^T + bias) + delta``.
+    Backward: ``dx`` gets the undropped base path ``dy W`` plus the dropped path
+    ``(d_base W + d_xa A) * keep_scale``.
+    """
+    xd = _op(np.multiply, dtype, x, keep_scale)
+    res = _matmul(x, W.T, dtype)
+    if bias is not None:
+        res = _op(np.add, dtype, res, bias[None, :])
+    base = _matmul(xd, W.T, dtype)
+    norm, _ = weight_norm_factored(W, A, B, scale, dtype)
+    eps = 1e-12 if dtype == "fp32" else 1e-6
+    nc = np.maximum(norm, round_to(np.float32(eps), dtype))
+    g = _op(np.divide, dtype, m[None, :], nc[None, :])
+    xa = _matmul(xd, A.T, dtype)
+    lora = _matmul(xa, B.T, dtype)
+    delta = compose_eager(lora, base, g, scale, dtype, dtype)
+    y = _op(np.add, dtype, res, delta)
+    d_lora, d_base, d_g = compose_backward_eager(dy, lora, base, g, scale, dtype, dtype)
+    dm = _op(np.divide, dtype, d_g[0], nc)
+    dB = _matmul(d_lora.T, xa, dtype)
+    d_xa = _matmul(d_lora, B, dtype)
+    dA = _matmul(d_xa.T, xd, dtype)
+    d_xd = _op(np.add, dtype, _matmul(d_base, W, dtype), _matmul(d_xa, A, dtype))
+    dx = _op(np.add, dtype, _matmul(dy, W, dtype), _op(np.multiply, dtype, d_xd, keep_scale))
+    return {"y": y, "delta": delta, "norm": norm, "g": g, "dx": dx, "dA": dA, "dB": dB, "dm": dm}
+
+
 # ---------------------------------------------------------------------------
 # Convolution / embedding norms and merge (the next rows beside the linear path)
 # ---------------------------------------------------------------------------

@@ -1,7 +1,7 @@
 """The measurement side of bench.py on CPU: the algorithmic work it rates kernels
 against (FLOPs of the factored norm, bytes of the compose kernels), the peak and
 DRAM-traffic lookups behind `roofline`, the workload description, and the CPU
-baseline's extrapolation.  No GPU work."""
+arms' thread count and full-workload estimate.  No GPU work."""
 
 import importlib.util
 import json
@@ -54,9 +54,15 @@ def test_peaks_and_traffic_lookups(bench):
     assert bench.read_traffic("no_such_kernel") is None
 
 
-def test_cpu_baseline_extrapolation(bench):
-    # One full-weight norm plus a forward/backward over CPU_SAMPLE_TOKENS tokens (which
-    # recomputes the norm): the token part scales to the full token count.
-    t_norm, t_step = 1.0, 3.0
-    full = t_norm + (t_step - t_norm) * (bench.TOKENS / bench.CPU_SAMPLE_TOKENS)
-    assert abs(bench.cpu_tokens_per_s(t_norm, t_step) - bench.TOKENS / full) < 1e-6
+def test_cpu_full_workload_extrapolation(bench):
+    # A step on a token sample includes one factored norm: only the token part scales.
+    t_norm, t_step, tokens = 1.0, 3.0, 4096
+    est = bench.extrapolate_full_step(t_norm, t_step, tokens)
+    assert abs(est - (1.0 + 2.0 * bench.TOKENS / tokens)) < 1e-12
+    assert bench.extrapolate_full_step(2.0, 1.0, tokens) == 2.0  # never below the norm alone
+
+
+def test_cpu_threads_follow_affinity_not_omp(bench, monkeypatch):
+    # torchrun exports OMP_NUM_THREADS=1; the host-core arms use every thread they may.
+    monkeypatch.setenv("OMP_NUM_THREADS", "1")
+    assert bench.cpu_threads() == len(os.sched_getaffinity(0))

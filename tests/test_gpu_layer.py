@@ -220,3 +220,107 @@ def test_row_sharded_single_rank_matches_dora_linear():
             assert_close(to_np(a), to_np(b), 1e-2, k)
     finally:
         dist.destroy_process_group()
+
+
+class _FixedKeep(torch.nn.Module):
+    """Dropout with a fixed mask: ``x * keep`` (keep is 0 or 1/(1-p) per element)."""
+
+    def __init__(self, keep):
+        super().__init__()
+        self.keep = keep
+
+    def forward(self, x):
+        return x * self.keep
+
+
+@pytest.mark.parametrize("dtype,bias", [("bf16", False), ("bf16", True), ("fp32", True)])
+def test_dora_linear_dropout_path_vs_oracle(dtype, bias):
+    """Training with LoRA dropout (the base_result=None path, dora.py:1155-1263 /
+    1470-1484, wired as variants.py:228-232): y, dx, dA, dB and dm against the
+    oracle for the same fixed dropout mask."""
+    from dorafactors_b200.layer import DoraLinear
+
+    T, in_f, out_f, r, s, p = 192, 384, 448, 16, 2.0, 0.2
+    rng = np.random.default_rng(41 + bias)
+    W = orc.round_to(rng.standard_normal((out_f, in_f)) * 0.02, dtype)
+    bvec = orc.round_to(rng.standard_normal(out_f) * 0.1, dtype) if bias else None
+    A = orc.round_to(rng.uniform(-1, 1, (r, in_f)) / np.sqrt(in_f), dtype)
+    B = orc.round_to(rng.standard_normal((out_f, r)) * 0.02, dtype)
+    x = orc.round_to(rng.standard_normal((T, in_f)), dtype)
+    dy = orc.round_to(rng.standard_normal((T, out_f)), dtype)
+    keep = orc.round_to((rng.uniform(0, 1, (T, in_f)) >= p) / (1.0 - p), dtype)
+    tdt = to_dev(W, dtype).dtype
+    base = torch.nn.Linear(in_f, out_f, bias=bias, device="cuda", dtype=tdt)
+    with torch.no_grad():
+        base.weight.copy_(to_dev(W, dtype))
+        if bias:
+            base.bias.copy_(to_dev(bvec, dtype))
+    mod = DoraLinear(base, r=r, scaling=s, dropout=p)
+    mod.lora_dropout = _FixedKeep(to_dev(keep, dtype))
+    with torch.no_grad():
+        mod.lora_A.weight.copy_(to_dev(A, dtype))
+        mod.lora_B.weight.copy_(to_dev(B, dtype))
+        mod.reset_magnitude()
+        mod.lora_magnitude_vector.weight.mul_(1.0 + 0.1 * torch.randn(out_f, device="cuda").to(tdt))
+    m = to_np(mod.lora_magnitude_vector.weight)
+    mod.train()
+    tx = to_dev(x, dtype).requires_grad_(True)
+    y = mod(tx)
+    y.backward(to_dev(dy, dtype))
+    ref = orc.dora_linear_dropout_forward_backward(x, keep, W, bvec, A, B, m, s, dy, dtype)
+    for k, v in (("y", y), ("dx", tx.grad), ("dA", mod.lora_A.weight.grad), ("dB", mod.lora_B.weight.grad),
+                 ("dm", mod.lora_magnitude_vector.weight.grad)):
+        assert_close(to_np(v), ref[k], RTOL[dtype], f"dropout {dtype} bias={bias} {k}")
+
+
+def test_dora_linear_headline_shape_vs_fp32():
+    """The benchmarked layer shape (W0 28672 x 8192 bf16, r = 384, s = 1.0) on 2048
+    tokens: the native forward + backward against an fp32 PyTorch evaluation of the
+    reference's eager formulas on the same GPU -- the dense row norm ||W0 + s B A||
+    (dora.py:1012-1022), g = m / norm, the eager compose g*(s*lora) + (g-1)*base
+    (dora.py:1331-1334), y = result + delta, and autograd for dx, dA, dB, dm with
+    the norm held constant.  Tolerance 1e-2 (normwise), the bf16 parity bar."""
+    import math
+
+    from dorafactors_b200.layer import DoraLinear
+
+    out_f, in_f, r, T, s = 28672, 8192, 384, 2048, 1.0
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(7)
+    base = torch.nn.Linear(in_f, out_f, bias=False, device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        base.weight.copy_((torch.randn(out_f, in_f, device=dev, generator=g) * 0.02).bfloat16())
+    mod = DoraLinear(base, r=r, scaling=s, init_lora_B_zero=False)
+    with torch.no_grad():
+        mod.lora_A.weight.copy_(((torch.rand(r, in_f, device=dev, generator=g) * 2 - 1) / math.sqrt(in_f))
+                                .bfloat16())
+        mod.lora_B.weight.copy_((torch.randn(out_f, r, device=dev, generator=g) * 0.01).bfloat16())
+        mod.reset_magnitude()
+        mod.lora_magnitude_vector.weight.mul_(1.0 + 0.05 * torch.randn(out_f, device=dev, generator=g).bfloat16())
+    x = torch.randn(T, in_f, device=dev, generator=g).bfloat16().requires_grad_(True)
+    dy = torch.randn(T, out_f, device=dev, generator=g).bfloat16()
+    y = mod(x)
+    y.backward(dy)
+    got = {"y": y.float(), "dx": x.grad.float(), "dA": mod.lora_A.weight.grad.float(),
+           "dB": mod.lora_B.weight.grad.float(), "dm": mod.lora_magnitude_vector.weight.grad.float()}
+    del y
+
+    # fp32 evaluation of the same step from the same bf16 values.
+    W = base.weight.detach().float()
+    A32 = mod.lora_A.weight.detach().float().requires_grad_(True)
+    B32 = mod.lora_B.weight.detach().float().requires_grad_(True)
+    m32 = mod.lora_magnitude_vector.weight.detach().float().requires_grad_(True)
+    x32 = x.detach().float().requires_grad_(True)
+    with torch.no_grad():
+        norm = (W + s * (B32 @ A32)).norm(dim=1)
+    gg = (m32 / norm.clamp_min(1e-12)).view(1, -1)
+    result = x32 @ W.T
+    lora = (x32 @ A32.T) @ B32.T
+    y32 = result + (gg * (s * lora) + (gg - 1) * result)
+    y32.backward(dy.float())
+    ref = {"y": y32.detach(), "dx": x32.grad, "dA": A32.grad, "dB": B32.grad, "dm": m32.grad}
+    native_norm = mod.lora_magnitude_vector._get_weight_norm_linear(
+        base_weight=base.weight, lora_A_w=mod.lora_A.weight, lora_B_w=mod.lora_B.weight, scaling=s)
+    assert_close(to_np(native_norm), to_np(norm), 1e-2, "headline norm")
+    for k in ("y", "dx", "dA", "dB", "dm"):
+        assert_close(to_np(got[k]), to_np(ref[k]), RTOL["bf16"], f"headline {k}")
