@@ -157,7 +157,8 @@ def physical_gpu_index(local_rank: int) -> int:
 class NativeTimer:
     """Wraps the native calls with CUDA events on the current stream while enabled."""
 
-    NAMES = ("weight_norm", "compose_fwd", "compose_bwd", "linear_output_fwd", "linear_output_bwd")
+    NAMES = ("weight_norm", "compose_fwd", "compose_bwd", "linear_output_fwd", "linear_output_bwd",
+             "linear_output_fwd_allgather", "linear_output_bwd_strided")
 
     def __init__(self):
         import torch
@@ -193,6 +194,9 @@ class NativeTimer:
                 ms = [s.elapsed_time(e) for s, e in evs]
                 out[n] = {"calls": len(ms), "avg_ms": sum(ms) / len(ms), "total_ms": sum(ms)}
         return out
+
+    def reset(self):
+        self.events = {n: [] for n in self.NAMES}
 
     def restore(self):
         for n in self.NAMES:
@@ -246,11 +250,13 @@ def run_native(args) -> None:
     x = x_dev.clone().requires_grad_(True)
     params = [mod.lora_A.weight, mod.lora_B.weight, mod.lora_magnitude_vector.weight]
 
-    def allreduce_grads():
-        if world > 1:
-            from dorafactors_b200.parallel import allreduce_grads as _allreduce
+    reducer = None
+    if world > 1:
+        from dorafactors_b200.parallel import GradAllReducer
 
-            _allreduce(params)
+        # Each gradient's all-reduce starts as soon as it is accumulated and runs
+        # under the rest of the backward (the base layer's dX GEMM).
+        reducer = GradAllReducer(params)
 
     def step(xin):
         for p in params:
@@ -258,7 +264,8 @@ def run_native(args) -> None:
         xin.grad = None
         y = mod(xin)
         y.backward(dy)
-        allreduce_grads()
+        if reducer is not None:
+            reducer.wait()
 
     def barrier():
         if world > 1:
@@ -337,6 +344,14 @@ def run_native(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms = float(t[0]), float(t[1])
 
+    # Extra measurements (not the headline value): the unfused drop-in wiring of
+    # the same layer, then the row-sharded 70B-class layer on both of its shapes.
+    dropin = None if args.no_extras else measure_dropin(mod, x, dy, params, reducer, timer, args, world, device)
+    del bufs, x_host
+    rowshard = None
+    if not args.no_extras:
+        rowshard = {f"{o}x{i}": measure_rowshard(o, i, args, world, rank, device, timer) for o, i in ROWSHARD_SHAPES}
+
     if rank == 0:
         peaks, peak_src = load_peaks()
         kernels = {}
@@ -391,13 +406,162 @@ def run_native(args) -> None:
             "clocks": clk,
             "peak_mem_gb": peak_mem / 1e9,
         }
+        if dropin is not None:
+            line["dropin_unfused"] = dropin
+        if rowshard is not None:
+            line["rowshard"] = rowshard
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(line), flush=True)
     timer.restore()
+    if reducer is not None:
+        reducer.remove()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _max_over_ranks(values: list[float], world: int, device) -> list[float]:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return values
+    t = torch.tensor(values, device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def measure_dropin(mod, x, dy, params, reducer, timer, args, world, device) -> dict:
+    """The same layer wired as PEFT's unchanged DoraLinearVariant.forward wires it
+    (variants.py:214-284): delta = DoraLinearLayer.forward(x, ..., base_result=result),
+    then a separate y = result + delta, and autograd adds d_y and d_base for the base
+    branch.  Timed like the headline step, for comparison with the fused layer output."""
+    import torch
+
+    layer = mod.lora_magnitude_vector
+
+    def step():
+        for p in params:
+            p.grad = None
+        x.grad = None
+        result = mod.base_layer(x)
+        delta = layer(x, lora_A=mod.lora_A, lora_B=mod.lora_B, scaling=SCALE, base_layer=mod.base_layer,
+                      base_result=result)
+        y = result + delta
+        y.backward(dy)
+        if reducer is not None:
+            reducer.wait()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    timer.reset()
+    timer.enabled = True
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    timer.enabled = False
+    (ms,) = _max_over_ranks([e0.elapsed_time(e1) / args.steps], world, device)
+    kern = {k: {"calls": v["calls"], "avg_ms": v["avg_ms"]} for k, v in timer.summary().items()}
+    return {"what": "DoraLinearLayer.forward (delta) + separate result + delta, unchanged PEFT variant wiring",
+            "ms_per_step": ms, "tokens_per_s": TOKENS * world / (ms * 1e-3), "kernels": kern}
+
+
+ROWSHARD_SHAPES = ((28672, 8192), (8192, 28672))
+ROWSHARD_RANK, ROWSHARD_TOKENS = 256, 32768
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this platform
+
+
+def measure_rowshard(out_f, in_f, args, world, rank, device, timer) -> dict:
+    """Out-feature row sharding of one 70B-class layer (strong scaling): W0 [out x in]
+    bf16 ~N(0, 0.02), r = 256, 32768 tokens ~N(0, 1), s = 1.0.  Every rank holds out/P
+    rows, runs the native norm and the fused compose + all-gather (its output columns
+    stored into every rank's buffer over NVLink), and in backward the strided fused
+    backward with the dX all-reduce overlapped.  Returns step time (max over ranks),
+    tokens/s and per-kernel rooflines."""
+    import math
+
+    import torch
+    import torch.distributed as dist
+
+    from dorafactors_b200 import _native
+    from dorafactors_b200.parallel import RowShardedDoraLinear
+
+    r, T, scale = ROWSHARD_RANK, ROWSHARD_TOKENS, 1.0
+    g = torch.Generator(device=device).manual_seed(4321)  # identical full tensors on every rank
+    W = (torch.randn(out_f, in_f, device=device, generator=g) * 0.02).bfloat16()
+    A = ((torch.rand(r, in_f, device=device, generator=g) * 2 - 1) / math.sqrt(in_f)).bfloat16()
+    B = (torch.randn(out_f, r, device=device, generator=g) * 0.01).bfloat16()
+    norm = torch.empty(out_f, dtype=torch.bfloat16, device=device)
+    _native.weight_norm(W, A, B, scale, norm)
+    layer = RowShardedDoraLinear.from_full(W, None, A, B, norm.clone(), scale)
+    del W, B
+    x = torch.randn(T, in_f, device=device, generator=g).bfloat16().requires_grad_(True)
+    dy = torch.randn(T, out_f, device=device, generator=g).bfloat16()
+    params = [layer.lora_A, layer.lora_B, layer.magnitude]
+
+    def step():
+        for p_ in params:
+            p_.grad = None
+        x.grad = None
+        y = layer(x)
+        y.backward(dy)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    timer.reset()
+    timer.enabled = True
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    timer.enabled = False
+    kern = timer.summary()
+    names = ("weight_norm", "linear_output_fwd_allgather", "linear_output_bwd_strided")
+    vals = _max_over_ranks([t0.elapsed_time(t1) / args.steps] + [kern.get(n, {}).get("avg_ms", 0.0) for n in names],
+                           world, device)
+    ms, k_ms = vals[0], dict(zip(names, vals[1:]))
+    peaks, _ = load_peaks()
+    w = layer.weight.shape[0]
+    e = 2
+    out = {"workload": f"row-sharded dora_linear_fwd_bwd out={out_f} in={in_f} r={r} tokens={T} bf16",
+           "ranks": world, "rows_per_rank": w, "scaling": "strong", "ms_per_step": ms,
+           "tokens_per_s": T / (ms * 1e-3), "kernels": {}}
+    if k_ms["weight_norm"] > 0:
+        f = norm_flops(w, in_f, r)
+        a = f / (k_ms["weight_norm"] * 1e-3) / 1e12
+        out["kernels"]["weight_norm"] = {"avg_ms": k_ms["weight_norm"], "algorithmic_flops": f, "achieved_tflops": a,
+                                         "frac": a / peaks["bf16_tflops_sustained"], "peak": "bf16 sustained"}
+    if k_ms["linear_output_fwd_allgather"] > 0:
+        t = k_ms["linear_output_fwd_allgather"] * 1e-3
+        # Local HBM: read lora + result, write inner + own y, plus the peers' columns
+        # landing in this rank's y; NVLink: this rank's columns to every peer.
+        hbm = e * T * w * 4 + e * T * w * (world - 1) + e * w
+        link = e * T * w * (world - 1)
+        bound = max(hbm / (peaks["hbm_gbs"] * 1e9), link / (NVLINK_GBS * 1e9))
+        out["kernels"]["compose_allgather"] = {
+            "avg_ms": k_ms["linear_output_fwd_allgather"], "hbm_bytes": hbm, "nvlink_bytes_out": link,
+            "hbm_gbs": hbm / t / 1e9, "allgather_gbs": link / t / 1e9, "bound": "nvlink" if link / NVLINK_GBS >
+            hbm / peaks["hbm_gbs"] else "hbm", "frac": bound / t,
+            "peaks": {"hbm_gbs": peaks["hbm_gbs"], "nvlink_gbs": NVLINK_GBS}}
+    if k_ms["linear_output_bwd_strided"] > 0:
+        b = compose_bwd_bytes(T, w)
+        a = b / (k_ms["linear_output_bwd_strided"] * 1e-3) / 1e9
+        out["kernels"]["linear_output_bwd"] = {"avg_ms": k_ms["linear_output_bwd_strided"], "algorithmic_bytes": b,
+                                               "achieved_gbs": a, "frac": a / peaks["hbm_gbs"]}
+    layer.pool.close()
+    del layer, x, dy
+    torch.cuda.empty_cache()
+    return out
 
 
 def read_traffic(kernel: str):
@@ -593,87 +757,46 @@ def run_reference(args) -> None:
 
 
 def run_rowshard(args) -> None:
-    """Out-feature row sharding of one 70B-class layer (strong scaling): W0 [out x in]
-    bf16, r = 256, 32768 tokens; every rank holds out/P rows, computes its norm and
-    compose locally and all-gathers the output (one NCCL all-gather per step)."""
+    """``--mode rowshard``: only the row-sharded 70B-class layer (``--shape``), one line."""
     import datetime
-    import math
 
     import torch
     import torch.distributed as dist
 
-    from dorafactors_b200 import _native
-    from dorafactors_b200.parallel import RowShardedDoraLinear
-
-    out_f, in_f = (int(v) for v in args.shape.split("x"))
-    r, T, scale = 256, 32768, 1.0
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29511")
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
-                            device_id=device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     torch.backends.cuda.matmul.allow_tf32 = False
-    g = torch.Generator(device=device).manual_seed(4321)  # identical full tensors on every rank
-    W = (torch.randn(out_f, in_f, device=device, generator=g) * 0.02).bfloat16()
-    A = ((torch.rand(r, in_f, device=device, generator=g) * 2 - 1) / math.sqrt(in_f)).bfloat16()
-    B = (torch.randn(out_f, r, device=device, generator=g) * 0.01).bfloat16()
-    norm = torch.empty(out_f, dtype=torch.bfloat16, device=device)
-    _native.weight_norm(W, A, B, scale, norm)
-    layer = RowShardedDoraLinear.from_full(W, None, A, B, norm.clone(), scale)
-    del W, B
-    x = torch.randn(T, in_f, device=device, generator=g).bfloat16().requires_grad_(True)
-    dy = torch.randn(T, out_f, device=device, generator=g).bfloat16()
-    params = [layer.lora_A, layer.lora_B, layer.magnitude]
-
-    def step():
-        for p_ in params:
-            p_.grad = None
-        x.grad = None
-        y = layer(x)
-        y.backward(dy)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        step()
-    t1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device=device)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms[0])
+    out_f, in_f = (int(v) for v in args.shape.split("x"))
+    timer = NativeTimer()
+    res = measure_rowshard(out_f, in_f, args, world, rank, device, timer)
+    timer.restore()
     if rank == 0:
-        shard_rows = layer.weight.shape[0]
         line = {
             "metric": METRIC,
-            "value": T / (ms * 1e-3),
+            "value": res["tokens_per_s"],
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": ms,
+            "ms_per_step": res["ms_per_step"],
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded normal / uniform weights, normal tokens)",
-            "config": {"workload": f"row-sharded dora_linear_fwd_bwd out={out_f} in={in_f} r={r} tokens={T} bf16",
-                       "out_features": out_f, "in_features": in_f, "rank": r, "tokens": T,
-                       "rows_per_rank": shard_rows, "allgather_bytes_per_step": T * out_f * 2,
-                       "parallelism": f"rowshard{world}"},
+            "config": {"workload": res["workload"], "out_features": out_f, "in_features": in_f,
+                       "rank": ROWSHARD_RANK, "tokens": ROWSHARD_TOKENS, "parallelism": f"rowshard{world}"},
+            "kernels": res["kernels"],
         }
         print(json.dumps(line), flush=True)
-    dist.barrier()
-    dist.destroy_process_group()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_model(args) -> None:
@@ -777,7 +900,9 @@ def main(argv=None) -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
-    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core oracle sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core reference sample")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the extra measurements (unfused drop-in wiring, row-sharded 70B-class layer)")
     ap.add_argument("--mode", choices=["dp", "rowshard", "model"], default="dp",
                     help="dp: token data parallelism (default); rowshard: out-feature sharding of one layer; "
                          "model: Llama-style decoder with DoRA on every projection")

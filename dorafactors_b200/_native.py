@@ -47,6 +47,14 @@ SIGNATURES = {
     "dora_linear_output_fwd": (_int, [_vp, _vp, _vp, _vp, _int, _dbl, _vp, _vp, _i64, _i64, _int, _vp]),
     "dora_linear_output_bwd": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _vp]),
     "dora_compose_bwd_noalloc": (_int, [_vp, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
+    "dora_linear_output_bwd_strided": (_int, [_vp, _i64, _vp, _vp, _int, _dbl, _vp, _vp, _vp, _vp, _sz, _i64, _i64,
+                                              _int, _vp]),
+    "dora_linear_output_fwd_allgather": (_int, [_vp, _vp, _vp, _vp, _int, _dbl, ctypes.POINTER(_vp), _int, _int,
+                                                _i64, _i64, _vp, _i64, _i64, _int, _vp]),
+    "dora_peer_buffer_alloc": (_int, [_sz, ctypes.POINTER(_vp), ctypes.c_char_p]),
+    "dora_peer_buffer_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "dora_peer_buffer_close": (_int, [_vp]),
+    "dora_peer_buffer_free": (_int, [_vp]),
     "dora_norm_assembly": (_int, [_vp, _vp, _vp, _dbl, _vp, _i64, _vp]),
     "dora_weight_norm_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int]),
     "dora_weight_norm": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _int, _dbl, _vp, _vp, _vp, _sz, _vp]),
@@ -257,6 +265,89 @@ def linear_output_bwd(d_y2d, inner2d, g1d, scale: float, d_lora2d, d_result2d, d
         ptr(d_g1d), ptr(ws), nbytes, rows, cols, act, stream_ptr(dev),
     )
     check(code, "dora_linear_output_bwd")
+
+
+def linear_output_bwd_strided(d_y_full, col_offset: int, cols: int, inner2d, g1d, scale: float, d_lora2d,
+                              d_result2d, d_g1d) -> None:
+    """Backward of one column shard whose d_y is columns [col_offset, col_offset + cols)
+    of the dense [rows x ld] ``d_y_full`` (read in place, no slice copy)."""
+    dev = d_y_full.device
+    rows, ld = d_y_full.shape
+    if d_y_full.stride(1) != 1 or d_y_full.stride(0) != ld:
+        raise ValueError("linear_output_bwd_strided: d_y must be a dense row-major matrix")
+    if not (0 <= col_offset and col_offset + cols <= ld):
+        raise ValueError(f"linear_output_bwd_strided: columns [{col_offset}, {col_offset + cols}) outside {ld}")
+    act = dtype_code(d_y_full)
+    ws, nbytes = (None, 0)
+    if d_g1d is not None:
+        ws, nbytes = bwd_workspace(dev, rows, cols, act)
+    base = ctypes.c_void_p(d_y_full.data_ptr() + col_offset * d_y_full.element_size())
+    code = load_library().dora_linear_output_bwd_strided(
+        base, ld, ptr(inner2d), ptr(g1d), dtype_code(g1d), float(scale), ptr(d_lora2d), ptr(d_result2d),
+        ptr(d_g1d), ptr(ws), nbytes, rows, cols, act, stream_ptr(dev),
+    )
+    check(code, "dora_linear_output_bwd_strided")
+
+
+def linear_output_fwd_allgather(lora2d, result2d, bias1d, g1d, scale: float, y_ptrs: list[int], rank: int,
+                                col_offset: int, ld: int, inner2d) -> None:
+    """This rank's columns of y = result + delta stored into every rank's [rows x ld]
+    output buffer (``y_ptrs[p]``: device addresses valid in this process)."""
+    dev = lora2d.device
+    rows, cols = lora2d.shape
+    arr = (ctypes.c_void_p * len(y_ptrs))(*[ctypes.c_void_p(int(p)) for p in y_ptrs])
+    code = load_library().dora_linear_output_fwd_allgather(
+        ptr(lora2d), ptr(result2d), ptr(bias1d), ptr(g1d), dtype_code(g1d), float(scale), arr, len(y_ptrs), rank,
+        col_offset, ld, ptr(inner2d), rows, cols, dtype_code(lora2d), stream_ptr(dev),
+    )
+    check(code, "dora_linear_output_fwd_allgather")
+
+
+PEER_HANDLE_BYTES = 64
+
+
+def peer_buffer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """cudaMalloc ``nbytes`` on the current device; returns (address, IPC handle)."""
+    p = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+    check(load_library().dora_peer_buffer_alloc(nbytes, ctypes.byref(p), h), "dora_peer_buffer_alloc")
+    return int(p.value), h.raw
+
+
+def peer_buffer_open(handle: bytes) -> int:
+    """Map another process's buffer; returns its address in this process."""
+    if len(handle) != PEER_HANDLE_BYTES:
+        raise ValueError(f"peer handle must be {PEER_HANDLE_BYTES} bytes")
+    p = ctypes.c_void_p()
+    check(load_library().dora_peer_buffer_open(handle, ctypes.byref(p)), "dora_peer_buffer_open")
+    return int(p.value)
+
+
+def peer_buffer_close(addr: int) -> None:
+    check(load_library().dora_peer_buffer_close(ctypes.c_void_p(addr)), "dora_peer_buffer_close")
+
+
+def peer_buffer_free(addr: int) -> None:
+    check(load_library().dora_peer_buffer_free(ctypes.c_void_p(addr)), "dora_peer_buffer_free")
+
+
+class _DeviceBytes:
+    """A device allocation seen by torch through __cuda_array_interface__ (bytes)."""
+
+    def __init__(self, addr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (addr, False),
+                                         "version": 3, "strides": None}
+
+
+def tensor_from_device_ptr(addr: int, shape: tuple, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A torch tensor over ``prod(shape)`` elements at ``addr`` (not owned by torch)."""
+    n = 1
+    for d in shape:
+        n *= int(d)
+    nbytes = n * torch.empty(0, dtype=dtype).element_size()
+    with torch.cuda.device(device):
+        raw = torch.as_tensor(_DeviceBytes(addr, nbytes), device=device)
+    return raw.view(dtype).view(*shape)
 
 
 def norm_assembly(w, c, b, scale: float, out) -> None:

@@ -23,7 +23,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libdora_b200.so")
-SOURCES = ["capi.cu", "compose.cu", "compose_ch.cu", "backward.cu", "norm_simt.cu", "norm_tc.cu", "norm_tc2.cu", "norm_sk.cu", "norm_sk2.cu", "norm.cu", "selftest.cu"]
+SOURCES = ["capi.cu", "compose.cu", "compose_ch.cu", "backward.cu", "norm_simt.cu", "norm_tc.cu", "norm_tc2.cu", "norm_sk.cu", "norm_sk2.cu", "norm.cu", "shard.cu", "peer.cu", "selftest.cu"]
 HEADERS = ["dora_common.cuh", "norm_internal.cuh", "tc_common.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-rdc=true", "--expt-relaxed-constexpr"]

@@ -20,11 +20,14 @@ namespace dora {
 // kRG selects the layer-output form: the second gradient is d_result = g * d_y
 // (the base branch of y = result + delta) instead of d_base = (g - 1) * d_out.
 // At most 80 registers (three 256-thread CTAs per SM): more loads in flight per SM.
-template <typename TA, typename TG, int VEC, bool kDL, bool kDB, bool kDG, bool kRG>
+// kLd: d_out rows are ld_d elements apart (a column slice of a wider gradient,
+// the row-sharded layer's share of the full d_y); every other array is dense.
+template <typename TA, typename TG, int VEC, bool kDL, bool kDB, bool kDG, bool kRG, bool kLd>
 __global__ void __launch_bounds__(256, 3)
 compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, const TG* __restrict__ g, float s,
                    TA* __restrict__ d_lora, TA* __restrict__ d_base, TG* __restrict__ d_g,
-                   unsigned* __restrict__ counters, float* __restrict__ partials, int64_t rows, int64_t vcols) {
+                   unsigned* __restrict__ counters, float* __restrict__ partials, int64_t rows, int64_t vcols,
+                   int64_t ld_d) {
   __shared__ float red[256 * VEC];
   __shared__ bool is_last;
   const int64_t vc = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -50,7 +53,7 @@ compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, c
           const int64_t rr = r + u * rstep;
           if (rr < rows) {
             const int64_t off = rr * cols + vc * VEC;
-            dv[u] = ld_stream(d_out + off);
+            dv[u] = ld_stream(d_out + (kLd ? rr * ld_d + vc * VEC : off));
             if constexpr (kDG) iv[u] = ld_stream(inner + off);
           }
         }
@@ -78,7 +81,7 @@ compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, c
         for (int u = 0; u < U; ++u) {
           const int64_t rr = r + u * rstep;
           if (rr < rows) {
-            df[u] = to_f32(d_out[rr * cols + vc]);
+            df[u] = to_f32(d_out[(kLd ? rr * ld_d : rr * cols) + vc]);
             if constexpr (kDG) xf[u] = to_f32(inner[rr * cols + vc]);
           }
         }
@@ -159,22 +162,23 @@ static BwdPlan bwd_plan(int64_t rows, int64_t cols, int esize, bool aligned) {
   return p;
 }
 
-template <typename TA, typename TG, int V, bool DL, bool DB, bool DG, bool RG>
+template <typename TA, typename TG, int V, bool DL, bool DB, bool DG, bool RG, bool LD>
 static void launch_bwd_v(const BwdPlan& p, const void* d_out, const void* inner, const void* g, float s,
                          void* d_lora, void* d_base, void* d_g, unsigned* cnt, float* part, int64_t rows,
-                         cudaStream_t st) {
-  compose_bwd_kernel<TA, TG, V, DL, DB, DG, RG><<<p.sh.grid, p.sh.block, 0, st>>>(
+                         int64_t ld_d, cudaStream_t st) {
+  compose_bwd_kernel<TA, TG, V, DL, DB, DG, RG, LD><<<p.sh.grid, p.sh.block, 0, st>>>(
       static_cast<const TA*>(d_out), static_cast<const TA*>(inner), static_cast<const TG*>(g), s,
-      static_cast<TA*>(d_lora), static_cast<TA*>(d_base), static_cast<TG*>(d_g), cnt, part, rows, p.vcols);
+      static_cast<TA*>(d_lora), static_cast<TA*>(d_base), static_cast<TG*>(d_g), cnt, part, rows, p.vcols, ld_d);
 }
 
-template <typename TA, typename TG, int V, bool RG>
+template <typename TA, typename TG, int V, bool RG, bool LD>
 static void launch_bwd_sel(const BwdPlan& p, const void* d_out, const void* inner, const void* g, float s,
                            void* d_lora, void* d_base, void* d_g, unsigned* cnt, float* part, int64_t rows,
-                           cudaStream_t st) {
+                           int64_t ld_d, cudaStream_t st) {
   const int sel = (d_lora ? 4 : 0) | (d_base ? 2 : 0) | (d_g ? 1 : 0);
 #define DORA_BWD_CASE(n, a, b, c) \
-  case n: launch_bwd_v<TA, TG, V, a, b, c, RG>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st); break;
+  case n: launch_bwd_v<TA, TG, V, a, b, c, RG, LD>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, \
+                                                   ld_d, st); break;
   switch (sel) {
     DORA_BWD_CASE(1, false, false, true)
     DORA_BWD_CASE(2, false, true, false)
@@ -188,11 +192,13 @@ static void launch_bwd_sel(const BwdPlan& p, const void* d_out, const void* inne
 #undef DORA_BWD_CASE
 }
 
-template <typename TA, typename TG, bool RG>
+template <typename TA, typename TG, bool RG, bool LD = false>
 static int launch_bwd(const void* d_out, const void* inner, const void* g, float s, void* d_lora, void* d_base,
-                      void* d_g, void* ws, size_t ws_bytes, int64_t rows, int64_t cols, cudaStream_t st) {
+                      void* d_g, void* ws, size_t ws_bytes, int64_t rows, int64_t cols, cudaStream_t st,
+                      int64_t ld_d = 0) {
+  constexpr int V = 16 / sizeof(TA);
   const bool aligned = aligned16(d_out) && (!inner || aligned16(inner)) && (!d_lora || aligned16(d_lora)) &&
-                       (!d_base || aligned16(d_base));
+                       (!d_base || aligned16(d_base)) && (!LD || ld_d % V == 0);
   BwdPlan p = bwd_plan(rows, cols, sizeof(TA), aligned);
   unsigned* cnt = nullptr;
   float* part = nullptr;
@@ -202,9 +208,8 @@ static int launch_bwd(const void* d_out, const void* inner, const void* g, float
     cnt = static_cast<unsigned*>(ws);
     part = reinterpret_cast<float*>(static_cast<char*>(ws) + p.counter_bytes);
   }
-  constexpr int V = 16 / sizeof(TA);
-  if (p.vec) launch_bwd_sel<TA, TG, V, RG>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st);
-  else launch_bwd_sel<TA, TG, 1, RG>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, st);
+  if (p.vec) launch_bwd_sel<TA, TG, V, RG, LD>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, ld_d, st);
+  else launch_bwd_sel<TA, TG, 1, RG, LD>(p, d_out, inner, g, s, d_lora, d_base, d_g, cnt, part, rows, ld_d, st);
   return check_launch();
 }
 
@@ -223,12 +228,13 @@ extern "C" size_t dora_compose_bwd_workspace_size(int64_t rows, int64_t cols, in
 
 namespace dora {
 
-template <bool RG>
+template <bool RG, bool LD = false>
 static int bwd_entry(const void* d_out, const void* inner, const void* g, int g_dtype, double scale, void* d_lora,
                      void* d_base, void* d_g, void* workspace, size_t workspace_bytes, int64_t rows, int64_t cols,
-                     int act_dtype, void* stream) {
+                     int act_dtype, void* stream, int64_t ld_d = 0) {
   if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
   if (g_dtype != act_dtype && g_dtype != DORA_DTYPE_F32) return DORA_ERR_INVALID_ARGUMENT;
+  if (LD && ld_d < cols) return DORA_ERR_INVALID_ARGUMENT;
   if (!d_lora && !d_base && !d_g) return DORA_OK;
   if (rows == 0 || cols == 0) {
     // Empty activations (their pointers may be null, as PyTorch gives for zero
@@ -247,19 +253,19 @@ static int bwd_entry(const void* d_out, const void* inner, const void* g, int g_
   switch (act_dtype) {
     case DORA_DTYPE_BF16:
       return g_dtype == DORA_DTYPE_F32
-                 ? launch_bwd<__nv_bfloat16, float, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
-                                                        workspace_bytes, rows, cols, st)
-                 : launch_bwd<__nv_bfloat16, __nv_bfloat16, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
-                                                                workspace_bytes, rows, cols, st);
+                 ? launch_bwd<__nv_bfloat16, float, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
+                                                            workspace_bytes, rows, cols, st, ld_d)
+                 : launch_bwd<__nv_bfloat16, __nv_bfloat16, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g,
+                                                                    workspace, workspace_bytes, rows, cols, st, ld_d);
     case DORA_DTYPE_F16:
       return g_dtype == DORA_DTYPE_F32
-                 ? launch_bwd<__half, float, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes,
-                                                 rows, cols, st)
-                 : launch_bwd<__half, __half, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
-                                                  workspace_bytes, rows, cols, st);
+                 ? launch_bwd<__half, float, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
+                                                     workspace_bytes, rows, cols, st, ld_d)
+                 : launch_bwd<__half, __half, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
+                                                      workspace_bytes, rows, cols, st, ld_d);
     default:
-      return launch_bwd<float, float, RG>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes, rows,
-                                          cols, st);
+      return launch_bwd<float, float, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes,
+                                              rows, cols, st, ld_d);
   }
 }
 
@@ -278,6 +284,14 @@ extern "C" int dora_linear_output_bwd(const void* d_y, const void* inner, const 
                                       void* stream) {
   return bwd_entry<true>(d_y, inner, g, g_dtype, scale, d_lora, d_result, d_g, workspace, workspace_bytes, rows,
                          cols, act_dtype, stream);
+}
+
+extern "C" int dora_linear_output_bwd_strided(const void* d_y, int64_t ld_dy, const void* inner, const void* g,
+                                              int g_dtype, double scale, void* d_lora, void* d_result, void* d_g,
+                                              void* workspace, size_t workspace_bytes, int64_t rows, int64_t cols,
+                                              int act_dtype, void* stream) {
+  return bwd_entry<true, true>(d_y, inner, g, g_dtype, scale, d_lora, d_result, d_g, workspace, workspace_bytes,
+                               rows, cols, act_dtype, stream, ld_dy);
 }
 
 // ---------------------------------------------------------------------------

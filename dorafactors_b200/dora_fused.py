@@ -411,6 +411,52 @@ except Exception:  # pragma: no cover - very old torch
     _HAS_CUSTOM_OP = False
 
 
+# ---------------------------------------------------------------------------
+# The reference's op name and schema, peft::fused_dora_compose(Tensor lora,
+# Tensor base, Tensor mag_norm_scale, float scale) -> Tensor
+# (dora_fused.py:1366-1446), so code and compiled graphs that call
+# torch.ops.peft.fused_dora_compose keep working.  It is registered as a
+# CompositeImplicitAutograd kernel over the dora_b200 ops above: it runs above
+# autograd, so it can see whether the magnitude needs a gradient and save
+# ``inner`` only then (the reference's setup_context rule, dora_fused.py:1380-1397),
+# while forward and backward are the native kernels with their own autograd
+# and fake implementations.  When the reference's own module registered the
+# name first in this process, that registration is left in place.
+# ---------------------------------------------------------------------------
+_HAS_PEFT_OP = False
+_peft_lib = None
+
+
+def _peft_compose_impl(lora: torch.Tensor, base: torch.Tensor, mag_norm_scale: torch.Tensor,
+                       scale: float) -> torch.Tensor:
+    save_inner = bool(mag_norm_scale.requires_grad and torch.is_grad_enabled())
+    out, _ = torch.ops.dora_b200.fused_dora_compose_fwd(lora, base, mag_norm_scale, scale, save_inner)
+    return out
+
+
+def _register_peft_op() -> bool:
+    global _peft_lib
+    if not _HAS_CUSTOM_OP:
+        return False
+    try:
+        if hasattr(torch.ops.peft, "fused_dora_compose"):
+            return False
+    except Exception:  # pragma: no cover - namespace lookup failure means "absent"
+        pass
+    try:
+        lib = torch.library.Library("peft", "FRAGMENT")
+        lib.define("fused_dora_compose(Tensor lora, Tensor base, Tensor mag_norm_scale, float scale) -> Tensor")
+        lib.impl("fused_dora_compose", _peft_compose_impl, "CompositeImplicitAutograd")
+    except Exception:  # pragma: no cover - defined concurrently by another module
+        logger.debug("dora_b200: peft::fused_dora_compose registration failed", exc_info=True)
+        return False
+    _peft_lib = lib  # the registration lives as long as this Library object
+    return True
+
+
+_HAS_PEFT_OP = _register_peft_op()
+
+
 def fused_dora_compose_autograd(
     lora: torch.Tensor,
     base: torch.Tensor,
@@ -420,9 +466,13 @@ def fused_dora_compose_autograd(
     """Training-time compose with the fused backward (dora_fused.py:1449-1480).
 
     Eager mode uses ``FusedDoRAComposeFunction``; under ``torch.compile`` the
-    custom op ``dora_b200::fused_dora_compose_fwd`` is the opaque graph node.
+    reference's op ``peft::fused_dora_compose`` (native kernels underneath) is
+    the graph node, or ``dora_b200::fused_dora_compose_fwd`` when that name
+    belongs to another registration.
     """
     if _is_dynamo_compiling() and _HAS_CUSTOM_OP:
+        if _HAS_PEFT_OP:
+            return torch.ops.peft.fused_dora_compose(lora, base, mag_norm_scale, scale)
         out, _ = torch.ops.dora_b200.fused_dora_compose_fwd(lora, base, mag_norm_scale, scale,
                                                             mag_norm_scale.requires_grad)
         return out

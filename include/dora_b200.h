@@ -8,6 +8,9 @@
  * them.  No entry point allocates device memory: scratch space is passed in
  * by the caller, sized by the matching *_workspace_size query.
  *
+ * The dora_peer_buffer_* functions are the exception: they allocate and map
+ * the peer-writable output buffers of the row-sharded layer.
+ *
  * Each entry point names the reference interface it replaces, as
  * file:line inside sockeye44/dorafactors, where "dora.py" and "dora_fused.py"
  * are code/peft_patched/src/peft/tuners/lora/{dora,dora_fused}.py.
@@ -151,6 +154,69 @@ int dora_linear_output_fwd(const void* lora, const void* result, const void* bia
 int dora_linear_output_bwd(const void* d_y, const void* inner, const void* g, int g_dtype, double scale,
                            void* d_lora, void* d_result, void* d_g, void* workspace, size_t workspace_bytes,
                            int64_t rows, int64_t cols, int act_dtype, void* stream);
+
+/*
+ * dora_linear_output_bwd with d_y read as a column slice of a wider gradient:
+ * row i of d_y starts ld_dy elements after row i-1 (ld_dy >= cols); inner,
+ * d_lora, d_result stay dense [rows x cols].  Same results and workspace rules
+ * as dora_linear_output_bwd.
+ *
+ * Replaces, for out-feature row sharding, the slice copy of the gathered
+ * output's gradient before the shard's backward; the reference has no tensor
+ * parallelism, so the arithmetic replaced is that of dora_linear_output_bwd
+ * (FusedDoRAComposeFunction.backward, dora_fused.py:1137-1206).
+ */
+int dora_linear_output_bwd_strided(const void* d_y, int64_t ld_dy, const void* inner, const void* g, int g_dtype,
+                                   double scale, void* d_lora, void* d_result, void* d_g, void* workspace,
+                                   size_t workspace_bytes, int64_t rows, int64_t cols, int act_dtype, void* stream);
+
+/*
+ * Row-sharded layer output with the output all-gather fused in.  This rank
+ * owns output columns [col_offset, col_offset + cols) of a layer whose full
+ * output y is [rows x ld] on every one of n_ranks ranks (1 .. 8).  It computes
+ * its columns of y = result + delta exactly as dora_linear_output_fwd (lora,
+ * result, inner and g are this rank's [rows x cols] / [cols] arrays) and
+ * stores each value into all n_ranks output buffers at its final position:
+ *   y_ranks[p][i * ld + col_offset + j] = y[i, j]     for every p.
+ * y_ranks is a host array of n_ranks device pointers valid in this process:
+ * y_ranks[rank] is this rank's own buffer, the others are peers' buffers
+ * mapped into this process (dora_peer_buffer_open, over NVLink).  No
+ * collective library call is made.  Ordering is the caller's: every rank must
+ * have finished reading the buffers before any rank calls this, and no rank
+ * may read them until every rank's call has completed (a cross-rank barrier
+ * on the stream before and after).
+ *
+ * Replaces, for out-feature row sharding of the adapted linear, the layer
+ * output compose (dora.py:1443-1468 with the result + delta of
+ * variants.py:244-283) followed by an NCCL all-gather of the shards and the
+ * permute that puts them in column order.  The reference has no tensor
+ * parallelism; the split rests on the row independence of its factored norm
+ * (dora.py:1024-1153) and of the compose (one g per output column).
+ */
+int dora_linear_output_fwd_allgather(const void* lora, const void* result, const void* bias, const void* g,
+                                     int g_dtype, double scale, void* const* y_ranks, int n_ranks, int rank,
+                                     int64_t col_offset, int64_t ld, void* inner, int64_t rows, int64_t cols,
+                                     int act_dtype, void* stream);
+
+/*
+ * Peer-writable output buffers for dora_linear_output_fwd_allgather (plain
+ * CUDA IPC, no multicast).  These have no counterpart in the reference, which
+ * has no tensor parallelism.
+ *
+ * dora_peer_buffer_alloc: cudaMalloc `bytes` on the current device and export
+ *   its IPC handle (DORA_PEER_HANDLE_BYTES bytes written to `handle`).
+ * dora_peer_buffer_open: map another process's exported buffer into this one
+ *   (peer access enabled on demand); *ptr is valid for kernels on the
+ *   current device.
+ * dora_peer_buffer_close: unmap a buffer opened with dora_peer_buffer_open.
+ * dora_peer_buffer_free: free a buffer from dora_peer_buffer_alloc; every
+ *   process that opened it must have closed it first.
+ */
+#define DORA_PEER_HANDLE_BYTES 64
+int dora_peer_buffer_alloc(size_t bytes, void** ptr, unsigned char* handle);
+int dora_peer_buffer_open(const unsigned char* handle, void** ptr);
+int dora_peer_buffer_close(void* ptr);
+int dora_peer_buffer_free(void* ptr);
 
 /*
  * Compose forward for convolution outputs: activations [batch, channels,

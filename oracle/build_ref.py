@@ -28,6 +28,8 @@ from __future__ import annotations
 
 import argparse
 import importlib
+import importlib.machinery
+import importlib.util
 import os
 import py_compile
 import sys
@@ -36,6 +38,7 @@ import textwrap
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 MODULES = ("dora", "dora_fused")
+BYTECODE_SUFFIX = ".refbc"
 REL_SRC = os.path.join("code", "peft_patched", "src", "peft", "tuners", "lora")
 
 _STUB_INTEGRATIONS = textwrap.dedent(
@@ -84,9 +87,9 @@ def build(reference_root: str | None = None) -> str | None:
     lora_dir = os.path.join(OUT, "peft", "tuners", "lora")
     os.makedirs(lora_dir, exist_ok=True)
     for m in MODULES:
-        # Sourceless bytecode placed where the module's .py would be: the import
-        # system loads it with SourcelessFileLoader, no source file needed.
-        py_compile.compile(os.path.join(src_dir, m + ".py"), cfile=os.path.join(lora_dir, m + ".pyc"),
+        # Bytecode only (no source file), under a name of its own: copy tools that
+        # drop *.pyc caches keep it, and load_reference() loads it explicitly.
+        py_compile.compile(os.path.join(src_dir, m + ".py"), cfile=os.path.join(lora_dir, m + BYTECODE_SUFFIX),
                            doraise=True, invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
     _write(os.path.join(OUT, "peft", "utils", "integrations.py"), _STUB_INTEGRATIONS)
     _write(os.path.join(OUT, "peft", "utils", "other.py"), _STUB_OTHER)
@@ -96,22 +99,37 @@ def build(reference_root: str | None = None) -> str | None:
 
 
 def available() -> bool:
-    return all(os.path.isfile(os.path.join(OUT, "peft", "tuners", "lora", m + ".pyc")) for m in MODULES)
+    return all(os.path.isfile(os.path.join(OUT, "peft", "tuners", "lora", m + BYTECODE_SUFFIX)) for m in MODULES)
 
 
 def load_reference():
     """Import the compiled reference modules; returns ``(dora, dora_fused)``.
 
-    ``peft`` resolves to ``oracle/_ref/peft`` (a namespace package), so this must
-    not run in a process that also imports a real ``peft``.
+    ``peft`` resolves to ``oracle/_ref/peft`` (a namespace package holding the
+    stub ``peft.utils``), so this must not run in a process that also imports a
+    real ``peft``.  ``dora_fused`` is loaded first: ``dora`` imports it by name.
     """
     if not available():
         raise ImportError("oracle/_ref is not built (python oracle/build_ref.py --reference <checkout>)")
     if OUT not in sys.path:
         sys.path.insert(0, OUT)
-    dora = importlib.import_module("peft.tuners.lora.dora")
-    dora_fused = importlib.import_module("peft.tuners.lora.dora_fused")
-    return dora, dora_fused
+    importlib.import_module("peft.tuners.lora")  # the namespace packages along the way
+    mods = {}
+    for m in ("dora_fused", "dora"):
+        name = f"peft.tuners.lora.{m}"
+        if name not in sys.modules:
+            path = os.path.join(OUT, "peft", "tuners", "lora", m + BYTECODE_SUFFIX)
+            loader = importlib.machinery.SourcelessFileLoader(name, path)
+            spec = importlib.util.spec_from_loader(name, loader)
+            mod = importlib.util.module_from_spec(spec)
+            sys.modules[name] = mod
+            try:
+                loader.exec_module(mod)
+            except BaseException:
+                del sys.modules[name]
+                raise
+        mods[m] = sys.modules[name]
+    return mods["dora"], mods["dora_fused"]
 
 
 def main(argv=None) -> None:

@@ -227,6 +227,52 @@ def test_custom_op_eager_and_opcheck():
     assert torch.equal(tl.grad, dl) and torch.equal(tb.grad, db) and torch.equal(tg.grad, dm)
 
 
+def test_peft_op_schema_eager_opcheck_and_compile():
+    """The reference's op name and schema, torch.ops.peft.fused_dora_compose(lora, base,
+    mag_norm_scale, scale) -> Tensor (dora_fused.py:1366-1446), served by the native
+    kernels: eager forward / backward equal the autograd Function bit for bit,
+    torch.library.opcheck passes, and a torch.compile'd function (Dynamo +
+    AOTAutograd, fullgraph) calling the op gives the same outputs and gradients."""
+    from dorafactors_b200 import dora_fused as df
+
+    assert df._HAS_PEFT_OP
+    op = torch.ops.peft.fused_dora_compose
+    assert str(op.default._schema) == (
+        "peft::fused_dora_compose(Tensor lora, Tensor base, Tensor mag_norm_scale, float scale) -> Tensor")
+    rng = np.random.default_rng(21)
+    lora, base = _rand(rng, (64, 512), "bf16"), _rand(rng, (64, 512), "bf16")
+    g = _rand(rng, (1, 512), "bf16", 0.5, 1.5)
+    dy = to_dev(_rand(rng, (64, 512), "bf16"), "bf16")
+
+    def leaves():
+        return (to_dev(lora, "bf16").requires_grad_(True), to_dev(base, "bf16").requires_grad_(True),
+                to_dev(g, "bf16").requires_grad_(True))
+
+    a = leaves()
+    ref = df.FusedDoRAComposeFunction.apply(*a, 1.25)
+    ref.backward(dy)
+    b = leaves()
+    out = op(*b, 1.25)
+    out.backward(dy)
+    assert torch.equal(out, ref)
+    for x, y in zip(b, a):
+        assert torch.equal(x.grad, y.grad)
+    # Frozen magnitude: no d_mag, same outputs.
+    with torch.no_grad():
+        assert torch.equal(op(to_dev(lora, "bf16"), to_dev(base, "bf16"), to_dev(g, "bf16"), 1.25), ref)
+    torch.library.opcheck(op.default, (*leaves(), 1.25))
+
+    def f(l, b_, m):
+        return torch.ops.peft.fused_dora_compose(l, b_, m, 1.25) * 2.0
+
+    c = leaves()
+    out_c = torch.compile(f, backend="aot_eager", fullgraph=True)(*c)
+    out_c.backward(dy)
+    assert torch.equal(out_c, ref * 2.0)
+    for x, y in zip(c, a):
+        assert_close(to_np(x.grad), to_np(y.grad) * 2.0, 1e-2, "compiled grad")
+
+
 def test_errors_are_loud():
     from dorafactors_b200 import dora_fused as df
 

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from _golden import RTOL, assert_close, load_group, to_dev, to_np
+from _golden import RTOL, assert_close, load_group, rel_errors, to_dev, to_np
 from oracle import dora_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -268,9 +268,20 @@ def test_dora_linear_dropout_path_vs_oracle(dtype, bias):
     y = mod(tx)
     y.backward(to_dev(dy, dtype))
     ref = orc.dora_linear_dropout_forward_backward(x, keep, W, bvec, A, B, m, s, dy, dtype)
+    # The same bf16 values evaluated at fp32 precision: the reference's bf16 eager
+    # d_mag rounds each of its two partial column sums (s*lora*dy and base*dy) to
+    # bf16 before adding them, which costs up to ~1% of the largest entry where
+    # they cancel; the native fp32 column sum of inner*dy does not.
+    exact = orc.dora_linear_dropout_forward_backward(x, keep, W, bvec, A, B, m, s, dy, "fp32")
     for k, v in (("y", y), ("dx", tx.grad), ("dA", mod.lora_A.weight.grad), ("dB", mod.lora_B.weight.grad),
                  ("dm", mod.lora_magnitude_vector.weight.grad)):
-        assert_close(to_np(v), ref[k], RTOL[dtype], f"dropout {dtype} bias={bias} {k}")
+        what = f"dropout {dtype} bias={bias} {k}"
+        if dtype == "fp32":
+            assert_close(to_np(v), ref[k], RTOL[dtype], what)
+        else:
+            l2, _ = rel_errors(to_np(v), ref[k])
+            assert l2 <= RTOL[dtype], f"{what} vs the bf16 eager oracle: rel-L2 {l2:.3e}"
+            assert_close(to_np(v), exact[k], RTOL[dtype], what + " vs fp32 evaluation")
 
 
 def test_dora_linear_headline_shape_vs_fp32():

@@ -1,6 +1,8 @@
 """Host-side logic of the drop-in modules, on CPU: argument checking, the
 no-fallback rule, compatibility knobs and shape helpers."""
 
+import os
+
 import pytest
 import torch
 
@@ -109,3 +111,26 @@ def test_dtype_codes_match_header():
     status = dict(re.findall(r"DORA_(OK|ERR_\w+) = (\d+)", hdr))
     assert int(status["ERR_INVALID_ARGUMENT"]) == _native.ERR_INVALID_ARGUMENT
     assert int(status["ERR_DEVICE_TIMEOUT"]) == _native.ERR_DEVICE_TIMEOUT
+
+
+def test_peft_op_schema_matches_reference():
+    """peft::fused_dora_compose is registered with the reference's schema
+    (dora_fused.py:1366-1446); checked in fresh processes so the two
+    registrations never meet."""
+    import subprocess
+    import sys
+
+    from oracle import build_ref
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ours = subprocess.run(
+        [sys.executable, "-c", "import torch; from dorafactors_b200 import dora_fused as df; "
+                               "print(df._HAS_PEFT_OP, torch.ops.peft.fused_dora_compose.default._schema)"],
+        cwd=root, capture_output=True, text=True, check=True).stdout.strip().splitlines()[-1]
+    assert ours.startswith("True peft::fused_dora_compose(")
+    if build_ref.available():
+        theirs = subprocess.run(
+            [sys.executable, "-c", "import torch; from oracle.build_ref import load_reference; load_reference(); "
+                                   "print(torch.ops.peft.fused_dora_compose.default._schema)"],
+            cwd=root, capture_output=True, text=True, check=True).stdout.strip().splitlines()[-1]
+        assert ours == "True " + theirs
