@@ -40,6 +40,7 @@ OUT_F, IN_F, RANK, TOKENS, SCALE = 28672, 8192, 384, 16384, 1.0
 METRIC = "DoRA layer fwd+bwd tokens/s, norm TFLOP/s & compose HBM GB/s vs peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 CPU_SAMPLE_TOKENS = 4096  # tokens per host-core step: a quarter of the workload's 16384
+CPU_PORT_TOKENS = 512  # the same with the numpy port (no reference build present)
 
 
 def workload_config(parallelism: str) -> dict:
@@ -621,8 +622,6 @@ class CpuLayerStep:
         W = (torch.randn(OUT_F, IN_F, generator=g) * 0.02).bfloat16()
         A = ((torch.rand(RANK, IN_F, generator=g) * 2 - 1) / math.sqrt(IN_F)).bfloat16()
         B = (torch.randn(OUT_F, RANK, generator=g) * 0.01).bfloat16()
-        x = torch.randn(tokens, IN_F, generator=g).bfloat16()
-        dy = torch.randn(tokens, OUT_F, generator=g).bfloat16()
         try:
             from oracle.build_ref import load_reference
 
@@ -631,6 +630,9 @@ class CpuLayerStep:
         except Exception as exc:  # oracle/_ref not built: fall back to the numpy port
             self.kind = "port"
             self.why_port = f"{type(exc).__name__}: {exc}"
+            self.tokens = tokens = min(tokens, CPU_PORT_TOKENS)  # numpy GEMMs: a smaller sample
+        x = torch.randn(tokens, IN_F, generator=g).bfloat16()
+        dy = torch.randn(tokens, OUT_F, generator=g).bfloat16()
         if self.kind == "reference":
             from torch import nn
 
@@ -699,9 +701,9 @@ def cpu_baseline_sample(steps: int = 3) -> dict:
     t = [c.step() for _ in range(steps)]
     t_step = sum(t) / len(t)
     t_norm = c.norm()
-    full = extrapolate_full_step(t_norm, t_step, CPU_SAMPLE_TOKENS)
+    full = extrapolate_full_step(t_norm, t_step, c.tokens)
     return {
-        "value": CPU_SAMPLE_TOKENS / t_step,
+        "value": c.tokens / t_step,
         "unit": "tokens/s",
         "cores": c.threads,
         "kind": c.kind,
@@ -709,7 +711,7 @@ def cpu_baseline_sample(steps: int = 3) -> dict:
         "ms_per_sample_step": t_step * 1e3,
         "extrapolated_full_workload": {"tokens_per_s": TOKENS / full, "ms_per_step": full * 1e3,
                                        "norm_ms": t_norm * 1e3,
-                                       "how": f"norm once + token part x {TOKENS}/{CPU_SAMPLE_TOKENS}"},
+                                       "how": f"norm once + token part x {TOKENS}/{c.tokens}"},
     }
 
 
@@ -727,8 +729,8 @@ def run_reference(args) -> None:
     times = [c.step() for _ in range(args.steps)]
     t_step = sum(times) / len(times)
     t_norm = c.norm()
-    full = extrapolate_full_step(t_norm, t_step, CPU_SAMPLE_TOKENS)
-    value = CPU_SAMPLE_TOKENS / t_step
+    full = extrapolate_full_step(t_norm, t_step, c.tokens)
+    value = c.tokens / t_step
     line = {
         "metric": METRIC,
         "value": value,
@@ -742,7 +744,7 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded normal / uniform weights, normal tokens)",
-        "config": {**workload_config("single"), "tokens_per_step_sampled": CPU_SAMPLE_TOKENS},
+        "config": {**workload_config("single"), "tokens_per_step_sampled": c.tokens},
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": c.threads, "kind": c.kind,
                          "sample": c.describe()},
@@ -751,7 +753,7 @@ def run_reference(args) -> None:
         "extrapolated_full_workload": {"tokens_per_s": TOKENS / full, "ms_per_step": full * 1e3,
                                        "norm_ms": t_norm * 1e3,
                                        "how": (f"estimate, not a measurement: the norm once + the measured "
-                                               f"token part x {TOKENS}/{CPU_SAMPLE_TOKENS}")},
+                                               f"token part x {TOKENS}/{c.tokens}")},
     }
     print(json.dumps(line), flush=True)
 

@@ -11,9 +11,17 @@
 //                      G's k-blocks with the B tile already staged in shared memory
 //   5. finalize        fixed-order partial sums + norm assembly + cast
 // fp16 runs step 4 on CUDA cores from the fp32 G (an fp16 hi/lo split could
-// overflow for large Gram entries); every other dtype mix runs steps 1, 3 and
-// 4 on CUDA cores.  The two-term split keeps about 16 significant bits of G,
-// so B G B^T carries a relative error near 2^-16 instead of bf16's 2^-8.
+// overflow for large Gram entries).  The two-term split keeps about 16
+// significant bits of G, so B G B^T carries a relative error near 2^-16
+// instead of bf16's 2^-8.
+//
+// Half-precision weights with fp32 adapters (PEFT's default: adapters upcast to
+// fp32 on a bf16 / fp16 base) first round the adapters into the weight dtype
+// (step 0, copies in the workspace) and then take the tensor-core path: each
+// adapter entry moves by at most half an ulp of the weight dtype, so the cross
+// and B G B^T terms carry a relative error of about that size, below the
+// rounding of the norm itself into the weight dtype.  fp32 weights run steps
+// 1, 3 and 4 on CUDA cores in fp32.
 #include <cstdlib>
 
 #include "norm_internal.cuh"
@@ -21,10 +29,11 @@
 namespace dora {
 
 struct NormPlan {
+  bool cast_a, cast_b;  // fp32 adapters rounded into the (half) weight dtype first
   bool tc_u, tc_v, tc_g, fuse_v, pair_u, sk_u, sk2_u;
   SkPlan sk;
   int gram_splits, u_splits, u_ntiles, v_splits, v_ntiles;
-  size_t off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, total;
+  size_t off_a, off_bh, off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, total;
 };
 
 static size_t up256(size_t x) { return (x + 255) / 256 * 256; }
@@ -79,10 +88,16 @@ static bool use_sk_kernel() {
   return on;
 }
 
+// `aligned`: W (and A / B where they are used in place) start on 16 bytes.
 static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, int bdt, bool aligned) {
   NormPlan p{};
   const int sms = num_sms();
-  const bool half_uniform = (wdt == adt && adt == bdt) && (wdt == DORA_DTYPE_BF16 || wdt == DORA_DTYPE_F16);
+  const bool half_w = wdt == DORA_DTYPE_BF16 || wdt == DORA_DTYPE_F16;
+  p.cast_a = half_w && adt == DORA_DTYPE_F32 && (bdt == DORA_DTYPE_F32 || bdt == wdt);
+  p.cast_b = half_w && bdt == DORA_DTYPE_F32 && (adt == DORA_DTYPE_F32 || adt == wdt);
+  if (p.cast_a) adt = wdt;
+  if (p.cast_b) bdt = wdt;
+  const bool half_uniform = (wdt == adt && adt == bdt) && half_w;
   p.tc_u = half_uniform && aligned && in % 8 == 0 && in > 0;
   p.tc_g = p.tc_u;
   p.tc_v = p.tc_u && wdt == DORA_DTYPE_BF16 && r % 8 == 0;
@@ -158,6 +173,8 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     p.v_splits = 1;
   }
   size_t o = 0;
+  p.off_a = o;     o += p.cast_a ? up256(size_t(r) * in * 2) : 0;
+  p.off_bh = o;    o += p.cast_b ? up256(size_t(out) * r * 2) : 0;
   p.off_gpart = o; o += up256(size_t(p.gram_splits) * r * r * 4);
   p.off_yt = o;    o += up256(size_t(r) * r * 4);
   p.off_hi = o;    o += up256(size_t(r) * r * 2);
@@ -193,13 +210,28 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
   if (!norm_out || (in_features > 0 && !W)) return DORA_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t M = out_features, K = in_features, R = rank;
+  int rc0;
   const bool lora_term = scale != 0.0 && R > 0 && K > 0;
   if (lora_term && (!A || !B)) return DORA_ERR_INVALID_ARGUMENT;
-  const bool aligned = aligned16(W) && (!lora_term || (aligned16(A) && aligned16(B)));
-  NormPlan p = make_plan(M, K, R, w_dtype, a_dtype, b_dtype, aligned);
+  NormPlan p = make_plan(M, K, R, w_dtype, a_dtype, b_dtype, true);
+  const bool aligned = aligned16(W) && (!lora_term || ((p.cast_a || aligned16(A)) && (p.cast_b || aligned16(B))));
+  if (!aligned) p = make_plan(M, K, R, w_dtype, a_dtype, b_dtype, false);
   if (!workspace || workspace_bytes < p.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return DORA_ERR_WORKSPACE;
   char* ws = static_cast<char*>(workspace);
+  if (lora_term && p.cast_a) {
+    // 0. fp32 adapters rounded into the weight dtype (workspace copies, 16-byte aligned).
+    launch_cast_to_half(static_cast<const float*>(A), ws + p.off_a, R * K, w_dtype, st);
+    if ((rc0 = check_launch())) return rc0;
+    A = ws + p.off_a;
+    a_dtype = w_dtype;
+  }
+  if (lora_term && p.cast_b) {
+    launch_cast_to_half(static_cast<const float*>(B), ws + p.off_bh, M * R, w_dtype, st);
+    if ((rc0 = check_launch())) return rc0;
+    B = ws + p.off_bh;
+    b_dtype = w_dtype;
+  }
   float* gpart = reinterpret_cast<float*>(ws + p.off_gpart);
   float* yt = reinterpret_cast<float*>(ws + p.off_yt);
   void* hi = ws + p.off_hi;

@@ -13,6 +13,8 @@ void simt_gemm(int dx, int dy, int dz, const void* X, int64_t ldx, const void* Y
                int64_t ldz, int64_t M, int64_t N, int64_t K, int ksplit, float* rowdot, float* sumsq, float* C,
                int64_t ldc, cudaStream_t st);
 void launch_row_sumsq(int dx, const void* X, int64_t M, int64_t K, float* out, cudaStream_t st);
+// fp32 -> half (bf16 / fp16) copy, round to nearest even.
+void launch_cast_to_half(const float* src, void* dst, int64_t n, int half_dtype, cudaStream_t st);
 // tri_tile > 0: the partials hold only the tiles (i <= j) of tri_tile x tri_tile
 // blocks; the lower blocks are read from their mirror images (G is symmetric).
 void launch_gram_reduce(const float* part, int nsplit, int64_t r, float* yt, int half_dtype, void* hi, void* lo,

@@ -309,6 +309,32 @@ template void simt_gemm<kGemmStore, false>(int, int, int, const void*, int64_t, 
                                            int64_t, int64_t, int64_t, int64_t, int, float*, float*, float*, int64_t,
                                            cudaStream_t);
 
+// fp32 -> bf16 / fp16, round to nearest even, four elements per thread and step.
+template <typename TH>
+__global__ void cast_to_half_kernel(const float* __restrict__ src, TH* __restrict__ dst, int64_t n, bool vec) {
+  const int64_t n4 = vec ? n / 4 : 0;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(src) + i);
+    TH h[4] = {from_f32<TH>(v.x), from_f32<TH>(v.y), from_f32<TH>(v.z), from_f32<TH>(v.w)};
+    *reinterpret_cast<uint2*>(dst + 4 * i) = *reinterpret_cast<const uint2*>(h);
+  }
+  for (int64_t i = 4 * n4 + int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    dst[i] = from_f32<TH>(src[i]);
+}
+
+void launch_cast_to_half(const float* src, void* dst, int64_t n, int half_dtype, cudaStream_t st) {
+  const bool vec = aligned16(src) && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0;
+  int64_t blocks = (n / 4 + 255) / 256;
+  const int64_t cap = int64_t(num_sms()) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  if (half_dtype == DORA_DTYPE_F16)
+    cast_to_half_kernel<<<unsigned(blocks), 256, 0, st>>>(src, static_cast<__half*>(dst), n, vec);
+  else
+    cast_to_half_kernel<<<unsigned(blocks), 256, 0, st>>>(src, static_cast<__nv_bfloat16*>(dst), n, vec);
+}
+
 void launch_row_sumsq(int dx, const void* X, int64_t M, int64_t K, float* out, cudaStream_t st) {
   const unsigned grid = unsigned((M + 7) / 8);
   switch (dx) {

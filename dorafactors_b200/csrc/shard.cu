@@ -19,8 +19,8 @@
 // Ordering with the peers is the caller's: every rank must be done reading
 // the output buffers before any rank calls this, and must not read them until
 // all ranks' calls have completed (a cross-rank barrier on the stream before
-// and after).  Each thread ends with a system-scope fence so its peer stores
-// are performed before anything the stream runs next.
+// and after).  With peers, each thread ends with a system-scope fence so its
+// peer stores are performed before anything the stream runs next.
 #include "dora_common.cuh"
 
 namespace dora {
@@ -99,7 +99,9 @@ compose_allgather_kernel(const TA* __restrict__ lora, const TA* __restrict__ res
       }
     }
   }
-  __threadfence_system();
+  // Peer stores are performed system-wide before this grid is seen to finish
+  // (only when there are peers: with one rank every store is local).
+  if (n_ranks > 1) __threadfence_system();
 }
 
 template <typename TA, typename TG, int V>

@@ -303,9 +303,10 @@ size_t dora_weight_norm_workspace_size(int64_t out_features, int64_t in_features
  * then the assembly of dora_norm_assembly and a cast to w_dtype (norm_out has
  * w_dtype).  When parts != NULL it receives 3*out floats: ||W0||^2, the cross
  * term and the B G B^T term, each [out] in fp32.  scale == 0 computes
- * sqrt(||W0||^2) only.  bf16 and fp16 weights with adapters of the same dtype
- * run on the tcgen05 tensor cores; every other dtype mix runs an fp32 CUDA-core
- * path.
+ * sqrt(||W0||^2) only.  bf16 and fp16 weights run on the tcgen05 tensor cores,
+ * with adapters of the weight dtype or fp32 (fp32 adapters are first rounded
+ * into the weight dtype in the workspace, an error below the norm's own
+ * rounding into that dtype); fp32 weights run an fp32 CUDA-core path.
  *
  * Replaces DoraLinearLayer._get_weight_norm_linear (dora.py:1024-1153) with
  * its fused_norm_assembly call (dora.py:1136-1148).

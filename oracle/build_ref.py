@@ -89,8 +89,11 @@ def build(reference_root: str | None = None) -> str | None:
     for m in MODULES:
         # Bytecode only (no source file), under a name of its own: copy tools that
         # drop *.pyc caches keep it, and load_reference() loads it explicitly.
+        # The code objects name the file by its path inside the reference project
+        # (tracebacks stay readable), not by a path of this machine.
         py_compile.compile(os.path.join(src_dir, m + ".py"), cfile=os.path.join(lora_dir, m + BYTECODE_SUFFIX),
-                           doraise=True, invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
+                           dfile=os.path.join(REL_SRC, m + ".py"), doraise=True,
+                           invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
     _write(os.path.join(OUT, "peft", "utils", "integrations.py"), _STUB_INTEGRATIONS)
     _write(os.path.join(OUT, "peft", "utils", "other.py"), _STUB_OTHER)
     with open(os.path.join(OUT, "SOURCE"), "w") as f:
@@ -114,6 +117,20 @@ def load_reference():
     if OUT not in sys.path:
         sys.path.insert(0, OUT)
     importlib.import_module("peft.tuners.lora")  # the namespace packages along the way
+    # The reference imports Triton when it can and then defines its @triton.jit
+    # kernels, which needs their source files; on CPU it never runs them
+    # (dora.py:928-958 gates the fused paths on is_cuda), so the modules are
+    # executed with Triton hidden and take their no-Triton branch.
+    hidden = {k: sys.modules.pop(k) for k in list(sys.modules) if k == "triton" or k.startswith("triton.")}
+    sys.modules["triton"] = None
+    try:
+        return _exec_reference_modules()
+    finally:
+        del sys.modules["triton"]
+        sys.modules.update(hidden)
+
+
+def _exec_reference_modules():
     mods = {}
     for m in ("dora_fused", "dora"):
         name = f"peft.tuners.lora.{m}"

@@ -134,15 +134,48 @@ def test_norm_scale_zero_and_rank_zero():
     assert np.all(parts[1] == 0) and np.all(parts[2] == 0)
 
 
-def test_norm_mixed_adapter_dtype():
-    """bf16 W0 with fp32 adapters (PEFT's default adapter dtype) takes the fp32 CUDA-core path."""
-    rng = np.random.default_rng(4)
-    W = orc.round_to(rng.standard_normal((256, 512)) * 0.02, "bf16")
-    A = (rng.uniform(-1, 1, (32, 512)) / np.sqrt(512)).astype(np.float32)
-    B = (rng.standard_normal((256, 32)) * 0.01).astype(np.float32)
-    n, _ = _native_norm(W, A, B, 2.0, "bf16", adt="fp32")
-    ref, _ = orc.weight_norm_factored(W, A, B, 2.0, "bf16")
-    assert _elem_rel(n, ref) <= 1e-2
+@pytest.mark.parametrize("wdt", ["bf16", "fp16"])
+@pytest.mark.parametrize("out_f,in_f,r,s", [(256, 512, 32, 2.0), (1000, 2048, 384, 0.5), (3000, 4104, 200, 1.0),
+                                           (512, 1000, 16, 3.0)])
+def test_norm_mixed_adapter_dtype(wdt, out_f, in_f, r, s):
+    """Half W0 with fp32 adapters (PEFT's default adapter dtype, dora.py:1061 computes
+    in fp32): the adapters are rounded into W0's dtype and the tensor-core path runs
+    (the CUDA-core path for in % 8 != 0).  Against the oracle's fp32 evaluation of
+    the fp32 adapters, at the parity bar; the fp32 terms within the adapters' own
+    rounding (2^-8 relative, normwise)."""
+    rng = np.random.default_rng(out_f + r)
+    W = orc.round_to(rng.standard_normal((out_f, in_f)) * 0.02, wdt)
+    A = (rng.uniform(-1, 1, (r, in_f)) / np.sqrt(in_f)).astype(np.float32)
+    B = (rng.standard_normal((out_f, r)) * 0.05).astype(np.float32)
+    n, parts = _native_norm(W, A, B, s, wdt, adt="fp32")
+    ref, rp = orc.weight_norm_factored(W, A, B, s, wdt)
+    assert _elem_rel(n, ref) <= RTOL[wdt]
+    assert_close(parts[0], rp["w_norm_sq"], 1e-5, "||W0||^2")
+    assert_close(parts[1], rp["cross"], 2.0**-8, "cross")
+    assert_close(parts[2], rp["ba"], 2.0**-8, "B G B^T")
+
+
+def test_norm_mixed_adapter_dtype_full_size():
+    """The benchmark layer (28672 x 8192, r = 384) with fp32 adapters on a bf16 W0:
+    against PyTorch fp32 GEMMs of the fp32 adapters on the same GPU."""
+    from dorafactors_b200 import _native
+
+    torch.manual_seed(1)
+    out_f, in_f, r = 28672, 8192, 384
+    W = (torch.randn(out_f, in_f, device="cuda") * 0.02).bfloat16()
+    A = (torch.rand(r, in_f, device="cuda") * 2 - 1) / in_f**0.5
+    B = torch.randn(out_f, r, device="cuda") * 0.01
+    norm = torch.empty(out_f, dtype=torch.bfloat16, device="cuda")
+    parts = torch.empty(3 * out_f, dtype=torch.float32, device="cuda")
+    _native.weight_norm(W, A, B, 1.0, norm, parts)
+    w, c, b = _torch_fp32_norm_parts(W, A, B)
+    p = parts.view(3, -1)
+    for got, ref, tol in ((p[0], w, 1e-5), (p[1], c, 2.0**-8), (p[2], b, 2.0**-8)):
+        rel = ((got.double() - ref.double()).norm() / ref.double().norm()).item()
+        assert rel <= tol, rel
+    ref_norm = torch.sqrt((w + 2 * c + b).clamp_min(0)).bfloat16()
+    rel = ((norm.float() - ref_norm.float()).abs() / ref_norm.float()).max().item()
+    assert rel <= 1e-2
 
 
 def _torch_fp32_norm_parts(W, A, B):
