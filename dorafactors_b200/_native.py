@@ -51,6 +51,7 @@ SIGNATURES = {
                                               _int, _vp]),
     "dora_linear_output_fwd_allgather": (_int, [_vp, _vp, _vp, _vp, _int, _dbl, ctypes.POINTER(_vp), _int, _int,
                                                 _i64, _i64, _vp, _i64, _i64, _int, _vp]),
+    "dora_linear_output_bias_grad": (_int, [_vp, _vp, _int, _vp, _i64, _i64, _int, _vp]),
     "dora_peer_buffer_alloc": (_int, [_sz, ctypes.POINTER(_vp), ctypes.c_char_p]),
     "dora_peer_buffer_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "dora_peer_buffer_close": (_int, [_vp]),
@@ -265,6 +266,15 @@ def linear_output_bwd(d_y2d, inner2d, g1d, scale: float, d_lora2d, d_result2d, d
         ptr(d_g1d), ptr(ws), nbytes, rows, cols, act, stream_ptr(dev),
     )
     check(code, "dora_linear_output_bwd")
+
+
+def linear_output_bias_grad(d_y2d, g1d, d_bias1d) -> None:
+    """d_bias = (1 - g) * column sums of d_y (the bias gradient of the fused layer output)."""
+    rows, cols = d_y2d.shape
+    code = load_library().dora_linear_output_bias_grad(
+        ptr(d_y2d), ptr(g1d), dtype_code(g1d), ptr(d_bias1d), rows, cols, dtype_code(d_y2d), stream_ptr(d_y2d.device),
+    )
+    check(code, "dora_linear_output_bias_grad")
 
 
 def linear_output_bwd_strided(d_y_full, col_offset: int, cols: int, inner2d, g1d, scale: float, d_lora2d,

@@ -295,6 +295,96 @@ extern "C" int dora_linear_output_bwd_strided(const void* d_y, int64_t ld_dy, co
 }
 
 // ---------------------------------------------------------------------------
+// Bias gradient of the layer-output form: y depends on the bias only through
+// base = result - bias, so d_bias[j] = -sum_i (g[j] - 1) * d_y[i, j]
+// = (1 - g[j]) * sum_i d_y[i, j].  One CTA per 64 columns (eight 16-byte
+// column vectors x 32 row lanes for 16-bit types), rows summed serially per
+// thread in fp32 and folded across the 32 lanes in a fixed order: deterministic,
+// no workspace, one read of d_y.
+// ---------------------------------------------------------------------------
+namespace dora {
+
+template <typename TA, typename TG, int VEC>
+__global__ void __launch_bounds__(256) bias_grad_kernel(const TA* __restrict__ d_y, const TG* __restrict__ g,
+                                                        TA* __restrict__ d_bias, int64_t rows, int64_t vcols) {
+  __shared__ float red[32][8 * VEC + 1];
+  const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;  // 8 column vectors x 32 row lanes
+  const int64_t vc = int64_t(blockIdx.x) * 8 + tx;
+  const int64_t cols = vcols * VEC;
+  float acc[VEC];
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) acc[k] = 0.f;
+  if (vc < vcols) {
+    for (int64_t r = ty; r < rows; r += 32) {
+      if constexpr (VEC > 1) {
+        float f[VEC];
+        Vec16<TA>::unpack(ld_stream(d_y + r * cols + vc * VEC), f);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] += f[k];
+      } else {
+        acc[0] += to_f32(d_y[r * cols + vc]);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) red[ty][tx * VEC + k] = acc[k];
+  __syncthreads();
+  if (threadIdx.x < 8 * VEC) {
+    const int j = threadIdx.x;
+    const int64_t c = int64_t(blockIdx.x) * 8 * VEC + j;
+    if (c < cols) {
+      float t = 0.f;
+      for (int y = 0; y < 32; ++y) t += red[y][j];
+      d_bias[c] = from_f32<TA>(__fmul_rn(__fsub_rn(1.0f, to_f32(g[c])), t));
+    }
+  }
+}
+
+template <typename TA, typename TG>
+static int launch_bias_grad(const void* d_y, const void* g, void* d_bias, int64_t rows, int64_t cols,
+                            cudaStream_t st) {
+  constexpr int V = 16 / sizeof(TA);
+  const bool vec = cols % V == 0 && aligned16(d_y);
+  const int64_t vcols = vec ? cols / V : cols;
+  const int64_t grid = (vcols + 7) / 8;
+  if (grid > int64_t(INT32_MAX)) return DORA_ERR_UNSUPPORTED;
+  if (vec)
+    bias_grad_kernel<TA, TG, V><<<unsigned(grid), 256, 0, st>>>(static_cast<const TA*>(d_y),
+                                                                 static_cast<const TG*>(g), static_cast<TA*>(d_bias),
+                                                                 rows, vcols);
+  else
+    bias_grad_kernel<TA, TG, 1><<<unsigned(grid), 256, 0, st>>>(static_cast<const TA*>(d_y),
+                                                                 static_cast<const TG*>(g), static_cast<TA*>(d_bias),
+                                                                 rows, vcols);
+  return check_launch();
+}
+
+}  // namespace dora
+
+extern "C" int dora_linear_output_bias_grad(const void* d_y, const void* g, int g_dtype, void* d_bias, int64_t rows,
+                                            int64_t cols, int act_dtype, void* stream) {
+  if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
+  if (g_dtype != act_dtype && g_dtype != DORA_DTYPE_F32) return DORA_ERR_INVALID_ARGUMENT;
+  if (cols == 0) return DORA_OK;
+  if (!d_bias || !g || (rows > 0 && !d_y)) return DORA_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    cudaError_t e = cudaMemsetAsync(d_bias, 0, size_t(cols) * dtype_size(act_dtype), st);
+    return e == cudaSuccess ? DORA_OK : set_cuda_error(e);
+  }
+  switch (act_dtype) {
+    case DORA_DTYPE_BF16:
+      return g_dtype == DORA_DTYPE_F32 ? launch_bias_grad<__nv_bfloat16, float>(d_y, g, d_bias, rows, cols, st)
+                                       : launch_bias_grad<__nv_bfloat16, __nv_bfloat16>(d_y, g, d_bias, rows, cols, st);
+    case DORA_DTYPE_F16:
+      return g_dtype == DORA_DTYPE_F32 ? launch_bias_grad<__half, float>(d_y, g, d_bias, rows, cols, st)
+                                       : launch_bias_grad<__half, __half>(d_y, g, d_bias, rows, cols, st);
+    default:
+      return launch_bias_grad<float, float>(d_y, g, d_bias, rows, cols, st);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Allocation-free variant of dora_compose_bwd.
 //
 // Some callers cannot hand this library a device workspace: a C or FFI host

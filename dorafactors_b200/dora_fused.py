@@ -281,6 +281,7 @@ class FusedDoRALinearOutputFunction(torch.autograd.Function):
         ctx.needs_mag = needs_mag
         ctx.scale = scale
         ctx.has_bias = bias is not None
+        ctx.bias_meta = (bias.shape, bias.dtype) if bias is not None else None
         if needs_mag:
             ctx.save_for_backward(inner, mag_norm_scale)
         else:
@@ -321,8 +322,12 @@ class FusedDoRALinearOutputFunction(torch.autograd.Function):
             d_g.zero_()
         d_bias = None
         if ctx.has_bias and ctx.needs_input_grad[4]:
-            # y depends on the bias directly through base = result - bias.
-            d_bias = -((g.float() - 1) * d.float().reshape(rows, cols)).sum(0)
+            # y depends on the bias directly through base = result - bias:
+            # d_bias = (1 - g) * column sums of d_y, one native pass over d_y.
+            d_bias = torch.empty(cols, dtype=d.dtype, device=d.device)
+            _native.linear_output_bias_grad(d.view(rows, cols), g, d_bias)
+            shape, dtype = ctx.bias_meta
+            d_bias = d_bias.view(shape).to(dtype)
         if d_lora is not None:
             d_lora = d_lora.view(d_y.shape)
         if d_result is not None:

@@ -156,6 +156,19 @@ int dora_linear_output_bwd(const void* d_y, const void* inner, const void* g, in
                            int64_t rows, int64_t cols, int act_dtype, void* stream);
 
 /*
+ * Gradient of dora_linear_output_fwd's bias (the bias enters y only through
+ * base = result - bias):
+ *   d_bias[j] = (1 - g[j]) * sum_i d_y[i,j]
+ * fp32 column sums in a fixed order (deterministic), one rounding into
+ * act_dtype; no workspace.  rows == 0 sets d_bias to zero.
+ *
+ * Replaces the autograd of `base_result - bias` in DoraLinearLayer.forward
+ * (dora.py:1443-1459), which sums the d_base tensor over the rows.
+ */
+int dora_linear_output_bias_grad(const void* d_y, const void* g, int g_dtype, void* d_bias, int64_t rows,
+                                 int64_t cols, int act_dtype, void* stream);
+
+/*
  * dora_linear_output_bwd with d_y read as a column slice of a wider gradient:
  * row i of d_y starts ld_dy elements after row i-1 (ld_dy >= cols); inner,
  * d_lora, d_result stay dense [rows x cols].  Same results and workspace rules

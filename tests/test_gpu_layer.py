@@ -335,3 +335,43 @@ def test_dora_linear_headline_shape_vs_fp32():
     assert_close(to_np(native_norm), to_np(norm), 1e-2, "headline norm")
     for k in ("y", "dx", "dA", "dB", "dm"):
         assert_close(to_np(got[k]), to_np(ref[k]), RTOL["bf16"], f"headline {k}")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
+def test_trainable_bias_gradient(dtype):
+    """A trainable base bias (PEFT's bias="all") on the fused layer-output path: the
+    native bias gradient (1 - g) * column sums of d_y, plus the base layer's own
+    d_result sum, must equal the oracle's total d_bias = column sums of d_y."""
+    from dorafactors_b200.layer import DoraLinear
+
+    T, in_f, out_f, r, s = 300, 256, 520, 16, 1.5
+    rng = np.random.default_rng(77)
+    W = orc.round_to(rng.standard_normal((out_f, in_f)) * 0.02, dtype)
+    bvec = orc.round_to(rng.standard_normal(out_f) * 0.1, dtype)
+    x = orc.round_to(rng.standard_normal((T, in_f)), dtype)
+    dy = orc.round_to(rng.standard_normal((T, out_f)), dtype)
+    tdt = to_dev(W, dtype).dtype
+    base = torch.nn.Linear(in_f, out_f, bias=True, device="cuda", dtype=tdt)
+    with torch.no_grad():
+        base.weight.copy_(to_dev(W, dtype))
+        base.bias.copy_(to_dev(bvec, dtype))
+    mod = DoraLinear(base, r=r, scaling=s, init_lora_B_zero=False)
+    base.bias.requires_grad_(True)
+    with torch.no_grad():
+        mod.lora_magnitude_vector.weight.mul_(1.0 + 0.2 * torch.randn(out_f, device="cuda").to(tdt))
+    y = mod(to_dev(x, dtype))
+    y.backward(to_dev(dy, dtype))
+    want = dy.astype(np.float64).sum(0)  # y = x W^T + b + delta(base = x W^T): dL/db = sum of d_y
+    assert_close(to_np(base.bias.grad), want, RTOL[dtype], f"{dtype} bias grad")
+    # The native piece alone: (1 - g) * sum_i d_y.
+    from dorafactors_b200 import _native
+
+    g = (torch.rand(out_f, device="cuda") + 0.5).to(tdt)
+    d = to_dev(dy, dtype)
+    got = torch.empty(out_f, dtype=tdt, device="cuda")
+    _native.linear_output_bias_grad(d, g, got)
+    ref = (1.0 - to_np(g).astype(np.float64)) * dy.astype(np.float64).sum(0)
+    assert_close(to_np(got), ref, RTOL[dtype], "native bias grad")
+    e = torch.empty(0, out_f, dtype=tdt, device="cuda")
+    _native.linear_output_bias_grad(e, g, got)
+    assert bool((got == 0).all())
