@@ -16,10 +16,23 @@ the timed steps.
 
 N > 1 (launched by torchrun, one process per GPU): token data parallelism.
 Every rank runs the full layer on its own 16384 tokens (weak scaling) and the
-LoRA / magnitude gradients are all-reduced over NCCL each step, the exchange
-data-parallel training performs.  ``--impl reference`` times the CPU
-restatement of the reference's eager path (the oracle) on the host cores, on a
-bounded token sample of the same workload, on rank 0 only.
+LoRA / magnitude gradients are all-reduced over NCCL each step, each one as
+soon as autograd has accumulated it, the exchange data-parallel training
+performs.
+
+Extra keys of the same line (not the headline value): ``dropin_unfused`` (the
+same layer wired as PEFT's unchanged DoraLinearVariant, delta then a separate
+``result + delta``), ``rowshard`` (the 70B-class layer, W0 28672 x 8192 and
+8192 x 28672, r=256, 32768 tokens, out-features sharded over the N ranks with
+the output all-gather fused into the compose, strong scaling) and, at 8 GPUs,
+``model`` (the Llama-style decoder with DoRA on all seven projections, one
+4096-token sequence per GPU, data parallel).
+
+``--impl reference`` times the reference's own eager CPU implementation (its
+``DoraLinearLayer`` from dora.py / dora_fused.py, byte-compiled into
+oracle/_ref by oracle/build_ref.py) on the host cores with every thread the
+process may use, each step a forward + backward on a 4096-token sample of the
+same workload over the full weight, on rank 0 only.
 """
 
 from __future__ import annotations
@@ -352,6 +365,10 @@ def run_native(args) -> None:
     rowshard = None
     if not args.no_extras:
         rowshard = {f"{o}x{i}": measure_rowshard(o, i, args, world, rank, device, timer) for o, i in ROWSHARD_SHAPES}
+    model = None
+    if not args.no_extras and world == MODEL_EXTRA_WORLD:
+        timer.enabled = False
+        model = measure_model(args.layers, args.seq, MODEL_EXTRA_STEPS, args.warmup, world, rank, local_rank, device)
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -411,6 +428,8 @@ def run_native(args) -> None:
             line["dropin_unfused"] = dropin
         if rowshard is not None:
             line["rowshard"] = rowshard
+        if model is not None:
+            line["model"] = model
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(line), flush=True)
@@ -801,31 +820,24 @@ def run_rowshard(args) -> None:
         dist.destroy_process_group()
 
 
-def run_model(args) -> None:
-    """Model-level configuration: a Llama-style decoder (hidden 4096, FFN 14336, 32
-    heads / 8 KV heads, vocab 128256; ``--layers`` of them, 32 by default) with DoRA
-    r=128, s=2.0 on q, k, v, o, gate, up and down, random weights; one sequence of
-    ``--seq`` random tokens per GPU (weak scaling), causal-LM loss, backward, DDP
-    all-reduce of the adapter gradients, fused AdamW step."""
-    import datetime
+MODEL_EXTRA_WORLD = 8  # the model-level configuration runs as an extra key at this many GPUs
+MODEL_EXTRA_STEPS = 5
 
+
+def measure_model(layers: int, seq: int, steps: int, warmup: int, world: int, rank: int, local_rank: int,
+                  device) -> dict:
+    """Model-level configuration: a Llama-style decoder (hidden 4096, FFN 14336, 32
+    heads / 8 KV heads, vocab 128256; ``layers`` of them) with DoRA r=128, s=2.0 on
+    q, k, v, o, gate, up and down, random weights; one sequence of ``seq`` random
+    tokens per GPU (weak scaling), causal-LM loss, backward, DDP all-reduce of the
+    adapter gradients, fused AdamW step.  Step time is the max over ranks."""
     import torch
     import torch.distributed as dist
 
     from dorafactors_b200 import _native
     from dorafactors_b200.model import add_dora, build_llama, llama_config
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    if world > 1:
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29512")
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=600),
-                                device_id=device)
-    cfg = llama_config(layers=args.layers)
+    cfg = llama_config(layers=layers)
     model = build_llama(cfg, device)
     params = add_dora(model, r=128, scaling=2.0)
     runner = model
@@ -833,7 +845,7 @@ def run_model(args) -> None:
         runner = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank])
     opt = torch.optim.AdamW(params, lr=1e-5, fused=True)
     g = torch.Generator(device=device).manual_seed(1000 + rank)
-    ids = torch.randint(0, cfg.vocab_size, (1, args.seq), device=device, generator=g)
+    ids = torch.randint(0, cfg.vocab_size, (1, seq), device=device, generator=g)
 
     def step():
         opt.zero_grad(set_to_none=True)
@@ -842,53 +854,77 @@ def run_model(args) -> None:
         opt.step()
         return loss
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(local_rank)
-    clocks.start()
+    torch.cuda.reset_peak_memory_stats(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = _native.launch_count()
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         loss = step()
     e1.record()
     torch.cuda.synchronize()
-    launches = (_native.launch_count() - launches0) // max(args.steps, 1) * args.steps
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
+    launches = _native.launch_count() - launches0
+    ms = e0.elapsed_time(e1) / steps
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
+    out = {"workload": f"llama-style decoder x{layers} (hidden 4096, ffn 14336, 32/8 heads, vocab 128256), "
+                       f"DoRA r=128 s=2 on q,k,v,o,gate,up,down, {seq} tokens per GPU",
+           "metric": "DoRA model training tokens/s (Llama-style, 7 adapted projections per layer)",
+           "n_gpus": world, "layers": layers, "seq_len": seq, "global_batch": world, "parallelism": f"dp{world}",
+           "steps": steps, "warmup": warmup, "ms_per_step": ms, "tokens_per_s": seq * world / (ms * 1e-3),
+           "trainable_params": sum(p.numel() for p in params), "loss": float(loss.detach()),
+           "native_launches_per_step": launches // max(steps, 1),
+           "peak_mem_gb": torch.cuda.max_memory_allocated(device) / 1e9}
+    del runner, model, opt, params
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_model(args) -> None:
+    """``--mode model``: only the model-level configuration, one line."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    clocks = ClockSampler(physical_gpu_index(local_rank))
+    clocks.start()
+    res = measure_model(args.layers, args.seq, args.steps, args.warmup, world, rank, local_rank, device)
+    clk = clocks.stop()
     if rank == 0:
-        n_train = sum(p.numel() for p in params)
         line = {
-            "metric": "DoRA model training tokens/s (Llama-style, 7 adapted projections per layer)",
-            "value": args.seq * world / (ms * 1e-3),
+            "metric": res["metric"],
+            "value": res["tokens_per_s"],
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": ms,
+            "ms_per_step": res["ms_per_step"],
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (random-init weights, uniform random token ids)",
-            "config": {"workload": f"llama-style decoder x{args.layers} (hidden 4096, ffn 14336, 32/8 heads, "
-                                   f"vocab 128256), DoRA r=128 s=2 on q,k,v,o,gate,up,down",
-                       "layers": args.layers, "global_batch": world, "seq_len": args.seq,
-                       "trainable_params": n_train, "parallelism": f"dp{world}",
-                       "l2": "activations far larger than L2, no flush needed"},
-            "loss": float(loss.detach()),
-            "gpu_launches": launches,
+            "config": {"workload": res["workload"], "layers": args.layers, "global_batch": world,
+                       "seq_len": args.seq, "trainable_params": res["trainable_params"],
+                       "parallelism": f"dp{world}", "l2": "activations far larger than L2, no flush needed"},
+            "loss": res["loss"],
+            "gpu_launches": res["native_launches_per_step"] * args.steps,
             "clocks": clk,
-            "peak_mem_gb": torch.cuda.max_memory_allocated(device) / 1e9,
+            "peak_mem_gb": res["peak_mem_gb"],
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -904,7 +940,8 @@ def main(argv=None) -> None:
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core reference sample")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the extra measurements (unfused drop-in wiring, row-sharded 70B-class layer)")
+                    help="skip the extra measurements (unfused drop-in wiring, row-sharded 70B-class layer, "
+                         "and at 8 GPUs the model-level configuration)")
     ap.add_argument("--mode", choices=["dp", "rowshard", "model"], default="dp",
                     help="dp: token data parallelism (default); rowshard: out-feature sharding of one layer; "
                          "model: Llama-style decoder with DoRA on every projection")

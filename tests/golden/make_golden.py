@@ -15,7 +15,7 @@ Output: ``tests/golden/*.npz``.  Half-precision tensors are stored as their raw
 ``uint16`` bit patterns under ``<name>__bf16`` / ``<name>__fp16`` keys, fp32 as
 float32.  Run from the repository root::
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 The fixtures are small (a few hundred KB in total) and committed; the reference
 is never read at test time.
@@ -426,7 +426,9 @@ def gen_merge_cases(dora) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DORA_REFERENCE_ROOT"),
+                    required="DORA_REFERENCE_ROOT" not in os.environ,
+                    help="reference checkout (default: $DORA_REFERENCE_ROOT)")
     ap.add_argument("--groups", default="", help="comma-separated subset of groups to (re)write")
     args = ap.parse_args()
     torch.manual_seed(0)
