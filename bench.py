@@ -24,7 +24,9 @@ Extra keys of the same line (not the headline value): ``dropin_unfused`` (the
 same layer wired as PEFT's unchanged DoraLinearVariant, delta then a separate
 ``result + delta``), ``rowshard`` (the 70B-class layer, W0 28672 x 8192 and
 8192 x 28672, r=256, 32768 tokens, out-features sharded over the N ranks with
-the output all-gather fused into the compose, strong scaling) and, at 8 GPUs,
+the output all-gather fused into the compose, strong scaling), at 1 GPU
+``rank_sweep`` (the factored norm on W0 8192 x 8192 for r = 16 .. 1024 and the
+compose kernels at 8192 x 8192, each call timed alone) and, at 8 GPUs,
 ``model`` (the Llama-style decoder with DoRA on all seven projections, one
 4096-token sequence per GPU, data parallel).
 
@@ -365,6 +367,10 @@ def run_native(args) -> None:
     rowshard = None
     if not args.no_extras:
         rowshard = {f"{o}x{i}": measure_rowshard(o, i, args, world, rank, device, timer) for o, i in ROWSHARD_SHAPES}
+    sweep = None
+    if not args.no_extras and world == 1:
+        timer.enabled = False
+        sweep = measure_rank_sweep(device)
     model = None
     if not args.no_extras and world == MODEL_EXTRA_WORLD:
         timer.enabled = False
@@ -430,6 +436,8 @@ def run_native(args) -> None:
             line["rowshard"] = rowshard
         if model is not None:
             line["model"] = model
+        if sweep is not None:
+            line["rank_sweep"] = sweep
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(line), flush=True)
@@ -489,6 +497,71 @@ def measure_dropin(mod, x, dy, params, reducer, timer, args, world, device) -> d
     kern = {k: {"calls": v["calls"], "avg_ms": v["avg_ms"]} for k, v in timer.summary().items()}
     return {"what": "DoraLinearLayer.forward (delta) + separate result + delta, unchanged PEFT variant wiring",
             "ms_per_step": ms, "tokens_per_s": TOKENS * world / (ms * 1e-3), "kernels": kern}
+
+
+SWEEP_RANKS = (16, 64, 128, 256, 512, 1024)
+SWEEP_DIM = 8192
+
+
+def measure_rank_sweep(device, iters: int = 10, warmup: int = 3) -> dict:
+    """Rank sweep on a fixed layer (W0 8192 x 8192 bf16 ~N(0, 0.02), r in 16..1024,
+    8192 tokens): the factored norm per rank, rated against HBM and the tensor pipe
+    (it crosses from HBM-bound to tensor-bound near r = 281), and the compose forward
+    and backward at 8192 x 8192.  Each call is timed alone with CUDA events after a
+    256 MB write that evicts L2 (W0, 134 MB, is about L2's size)."""
+    import math
+
+    import torch
+
+    from dorafactors_b200 import _native
+
+    peaks, _ = load_peaks()
+    n = SWEEP_DIM
+    g = torch.Generator(device=device).manual_seed(8192)
+    W = (torch.randn(n, n, device=device, generator=g) * 0.02).bfloat16()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def timed(fn) -> float:
+        for _ in range(warmup):
+            fn()
+        ms = []
+        for _ in range(iters):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            ms.append(s.elapsed_time(e))
+        return statistics.median(ms)
+
+    out = {"workload": f"W0 {n}x{n} bf16, r in {list(SWEEP_RANKS)}, {n} tokens; each call alone, L2 evicted",
+           "norm": {}}
+    for r in SWEEP_RANKS:
+        A = ((torch.rand(r, n, device=device, generator=g) * 2 - 1) / math.sqrt(n)).bfloat16()
+        B = (torch.randn(n, r, device=device, generator=g) * 0.01).bfloat16()
+        norm = torch.empty(n, dtype=torch.bfloat16, device=device)
+        ms = timed(lambda: _native.weight_norm(W, A, B, 1.0, norm))
+        f, b = norm_flops(n, n, r), norm_bytes(n, n, r)
+        tf, gbs = f / (ms * 1e-3) / 1e12, b / (ms * 1e-3) / 1e9
+        bound = "hbm" if f / b < peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9) else "tensor"
+        out["norm"][str(r)] = {"ms": ms, "gflop": f / 1e9, "tflops": tf, "tensor_frac": tf / peaks["bf16_tflops"],
+                               "bytes": b, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"], "bound": bound,
+                               "frac": gbs / peaks["hbm_gbs"] if bound == "hbm" else tf / peaks["bf16_tflops"]}
+    a = torch.randn(n, n, device=device, generator=g).bfloat16()
+    c = torch.randn(n, n, device=device, generator=g).bfloat16()
+    mag = (torch.rand(n, device=device, generator=g) + 0.5).bfloat16()
+    o1, o2, dg = torch.empty_like(a), torch.empty_like(a), torch.empty(n, dtype=torch.bfloat16, device=device)
+    for name, fn, nbytes in (
+        ("linear_output_fwd", lambda: _native.linear_output_fwd(a, c, None, mag, 1.0, o1, o2), compose_fwd_bytes(n, n)),
+        ("linear_output_bwd", lambda: _native.linear_output_bwd(a, c, mag, 1.0, o1, o2, dg), compose_bwd_bytes(n, n)),
+    ):
+        ms = timed(fn)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": ms, "bytes": nbytes, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]}
+    del W, flush, a, c, o1, o2
+    torch.cuda.empty_cache()
+    return out
 
 
 ROWSHARD_SHAPES = ((28672, 8192), (8192, 28672))
