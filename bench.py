@@ -507,8 +507,8 @@ def measure_rank_sweep(device, iters: int = 10, warmup: int = 3) -> dict:
     """Rank sweep on a fixed layer (W0 8192 x 8192 bf16 ~N(0, 0.02), r in 16..1024,
     8192 tokens): the factored norm per rank, rated against HBM and the tensor pipe
     (it crosses from HBM-bound to tensor-bound near r = 281), and the compose forward
-    and backward at 8192 x 8192.  Each call is timed alone with CUDA events after a
-    256 MB write that evicts L2 (W0, 134 MB, is about L2's size)."""
+    and backward at 8192 x 8192.  Calls are timed back to back with CUDA events after
+    a 256 MB write that evicts L2; W0 (134 MB) is larger than L2 (126 MB)."""
     import math
 
     import torch
@@ -524,18 +524,17 @@ def measure_rank_sweep(device, iters: int = 10, warmup: int = 3) -> dict:
     def timed(fn) -> float:
         for _ in range(warmup):
             fn()
-        ms = []
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
         for _ in range(iters):
-            flush.zero_()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
             fn()
-            e.record()
-            e.synchronize()
-            ms.append(s.elapsed_time(e))
-        return statistics.median(ms)
+        e.record()
+        e.synchronize()
+        return s.elapsed_time(e) / iters
 
-    out = {"workload": f"W0 {n}x{n} bf16, r in {list(SWEEP_RANKS)}, {n} tokens; each call alone, L2 evicted",
+    out = {"workload": f"W0 {n}x{n} bf16, r in {list(SWEEP_RANKS)}, {n} tokens; {iters} calls back to back "
+                       f"after an L2-evicting write",
            "norm": {}}
     for r in SWEEP_RANKS:
         A = ((torch.rand(r, n, device=device, generator=g) * 2 - 1) / math.sqrt(n)).bfloat16()
