@@ -618,6 +618,8 @@ def measure_rowshard(out_f, in_f, args, world, rank, device, timer) -> dict:
     torch.cuda.synchronize()
     timer.enabled = False
     kern = timer.summary()
+    if world == 1 and "linear_output_fwd" in kern:  # one shard: the plain layer-output kernel runs
+        kern["linear_output_fwd_allgather"] = kern.pop("linear_output_fwd")
     names = ("weight_norm", "linear_output_fwd_allgather", "linear_output_bwd_strided")
     vals = _max_over_ranks([t0.elapsed_time(t1) / args.steps] + [kern.get(n, {}).get("avg_ms", 0.0) for n in names],
                            world, device)

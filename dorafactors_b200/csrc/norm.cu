@@ -31,9 +31,10 @@ namespace dora {
 struct NormPlan {
   bool cast_a, cast_b;  // fp32 adapters rounded into the (half) weight dtype first
   bool tc_u, tc_v, tc_g, fuse_v, pair_u, sk_u, sk2_u;
+  bool fuse_g;  // r <= 16: Gram inside the stream-K kernel, B G B^T in the finalize
   SkPlan sk;
   int gram_splits, u_splits, u_ntiles, v_splits, v_ntiles;
-  size_t off_a, off_bh, off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, total;
+  size_t off_a, off_bh, off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, off_g16, total;
 };
 
 static size_t up256(size_t x) { return (x + 255) / 256 * 256; }
@@ -122,6 +123,12 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
   // Cross term: stream-K on CTA pairs (wide N tiles) or single CTAs; the split-K
   // kernels when neither applies (or when selected for comparison).
   p.fuse_v = p.tc_u && p.tc_v && tc_can_fuse_v(out, r, in);
+  // Low rank (r <= 16, one 16-column N tile): the stream-K kernel's row warps also add
+  // up the Gram matrix from the A tiles they already hold, and the finalize forms
+  // B G B^T on CUDA cores (256 FMAs per row), so the Gram, its reduce and the
+  // B G B^T units leave the launch sequence.
+  p.fuse_g = p.tc_u && r <= 16 && r % 8 == 0 && use_sk_kernel() && !use_pair_kernel() && sk2_mode() != 1;
+  if (p.fuse_g) p.fuse_v = false;
   if (p.tc_u) {
     const TcGemmShape u = tc_gemm_shape(out, r, in);
     TcGemmArgs probe{};
@@ -141,6 +148,7 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     const int m2 = sk2_mode();
     p.sk2_u = !p.pair_u && use_sk_kernel() && (m2 == 1 || (m2 < 0 && u.nt >= 256)) && tc2_sk_supported(probe);
     p.sk_u = !p.pair_u && !p.sk2_u && use_sk_kernel() && tc_sk_supported(probe);
+    if (p.fuse_g && !p.sk_u) p.fuse_g = false;  // the single-CTA stream-K kernel carries the Gram
     p.u_ntiles = u.n_tiles;
     if (p.sk2_u) {
       p.sk = tc2_sk_plan(out, r, in, p.fuse_v, sms);
@@ -182,6 +190,7 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
   p.off_w = o;     o += up256(size_t(p.u_splits) * out * 4);
   p.off_c = o;     o += up256(size_t(p.u_splits) * p.u_ntiles * out * 4);
   p.off_b = o;     o += up256(size_t(p.v_splits) * p.v_ntiles * out * 4);
+  p.off_g16 = o;   o += p.fuse_g ? up256(size_t(p.sk.grid) * 256 * 4) : 0;
   p.total = o;
   return p;
 }
@@ -248,6 +257,21 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
       if ((rc = check_launch())) return rc;
     }
     launch_norm_finalize(wpart, K > 0 ? 1 : 0, cpart, 0, bpart, 0, M, scale, w_dtype, norm_out, parts, st);
+    return check_launch();
+  }
+
+  if (p.fuse_g) {
+    // Low rank: cross term, ||W0||^2 and partial Grams in one stream-K launch, then the
+    // finalize with B G B^T.
+    float* g16 = reinterpret_cast<float*>(ws + p.off_g16);
+    TcGemmArgs u{};
+    u.dtype = w_dtype; u.X = W; u.Y1 = A; u.Y2 = nullptr; u.Z = B; u.ldz = R;
+    u.M = M; u.N = R; u.K = K; u.mode = kGemmRowdot; u.sumsq = true; u.k_splits = p.u_splits;
+    u.rowdot_part = cpart; u.sumsq_part = wpart; u.g_part = g16;
+    if (!tc_sk_supported(u)) return DORA_ERR_INVALID_ARGUMENT;
+    if ((rc = tc_sk_rowdot_gemm(u, p.sk, st))) return rc;
+    launch_norm_finalize_gram(wpart, p.u_splits, cpart, p.u_splits * p.u_ntiles, g16, p.sk.grid, int(R), B, b_dtype,
+                              M, scale, w_dtype, norm_out, parts, st);
     return check_launch();
   }
 

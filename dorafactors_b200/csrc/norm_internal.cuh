@@ -21,6 +21,11 @@ void launch_gram_reduce(const float* part, int nsplit, int64_t r, float* yt, int
                         int tri_tile, cudaStream_t st);
 void launch_norm_finalize(const float* wpart, int nw, const float* cpart, int nc, const float* bpart, int nb,
                           int64_t M, double scale, int out_dtype, void* norm_out, float* parts, cudaStream_t st);
+// Low-rank finalize: G = sum of ng partial 16 x 16 Grams (fixed order), B G B^T per row
+// on CUDA cores (r <= 16, B [M x r] in b_dtype), the slot sums and the assembly.
+void launch_norm_finalize_gram(const float* wpart, int nw, const float* cpart, int nc, const float* gpart, int ng,
+                               int r, const void* B, int b_dtype, int64_t M, double scale, int out_dtype,
+                               void* norm_out, float* parts, cudaStream_t st);
 
 // Tensor-core row-dot GEMM (norm_tc.cu).
 struct TcGemmArgs {
@@ -46,6 +51,9 @@ struct TcGemmArgs {
   // Store mode, M == N, symmetric product (the Gram matrix): 128 x 128 tiles and only
   // those with n_tile >= m_tile are computed; C's other tiles are left unwritten.
   bool tri = false;
+  // Stream-K kernel, N tile of 16 without the fused B G B^T phase: also emit partial
+  // Gram matrices A A^T, [grid][16 x 16] fp32 (one per CTA, fixed-order summable).
+  float* g_part = nullptr;
 };
 constexpr int kGramTile = 128;
 struct TcGemmShape {

@@ -218,6 +218,50 @@ __global__ void norm_finalize_kernel(const float* __restrict__ wpart, int nw, co
   }
 }
 
+// Low-rank finalize (r <= 16): G = sum over the stream-K CTAs' partial Grams in CTA
+// order (each CTA of this grid forms it in shared memory: 256 entries x ng partials),
+// then per row ba = B_j G B_j^T in fp32 (t_a = sum_b G_ab B_jb, ba = sum_a B_ja t_a,
+// the reference's rowsum((B @ G) * B), dora.py:1132-1134), the slot sums and the
+// assembly.
+template <typename TO, typename TB>
+__global__ void __launch_bounds__(256) norm_finalize_gram_kernel(
+    const float* __restrict__ wpart, int nw, const float* __restrict__ cpart, int nc,
+    const float* __restrict__ gpart, int ng, int r, const TB* __restrict__ B, int64_t M, float two_s, float s2,
+    TO* __restrict__ norm_out, float* __restrict__ parts) {
+  __shared__ float G[16][17];
+  pdl_wait();  // the partials come from the previous kernel
+  {
+    const int e = threadIdx.x;  // 256 threads, one Gram entry each
+    float t = 0.f;
+    for (int i = 0; i < ng; ++i) t += gpart[int64_t(i) * 256 + e];
+    G[e >> 4][e & 15] = t;
+  }
+  __syncthreads();
+  const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  float w = 0.f, c = 0.f;
+  for (int i = 0; i < nw; ++i) w += wpart[int64_t(i) * M + m];
+  for (int i = 0; i < nc; ++i) c += cpart[int64_t(i) * M + m];
+  float bj[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) bj[k] = k < r ? to_f32(B[m * r + k]) : 0.f;
+  float b = 0.f;
+#pragma unroll
+  for (int x = 0; x < 16; ++x) {
+    float t = 0.f;
+#pragma unroll
+    for (int y = 0; y < 16; ++y) t = fmaf(G[x][y], bj[y], t);
+    b = fmaf(bj[x], t, b);
+  }
+  const float n = assemble_one(w, c, b, two_s, s2);
+  norm_out[m] = from_f32<TO>(n);
+  if (parts) {
+    parts[m] = w;
+    parts[M + m] = c;
+    parts[2 * M + m] = b;
+  }
+}
+
 // get_weight_norm (dora.py:1012-1022): one warp per row.
 template <typename TW, typename TL>
 __global__ void dense_norm_kernel(const TW* __restrict__ W, const TL* __restrict__ L, float s, int64_t M, int64_t K,
@@ -376,6 +420,36 @@ void launch_norm_finalize(const float* wpart, int nw, const float* cpart, int nc
     default:
       e = launch_pdl(norm_finalize_kernel<float>, grid, block, 0, st, wpart, nw, cpart, nc, bpart, nb, M, two_s,
                      s2, sz, static_cast<float*>(norm_out), parts);
+      break;
+  }
+  if (e != cudaSuccess) set_cuda_error(e);
+}
+
+template <typename TO>
+static cudaError_t launch_finalize_gram_t(const float* wpart, int nw, const float* cpart, int nc, const float* gpart,
+                                          int ng, int r, const void* B, int b_dtype, int64_t M, float two_s, float s2,
+                                          void* norm_out, float* parts, cudaStream_t st) {
+  const dim3 grid(unsigned((M + 255) / 256)), block(256);
+  if (b_dtype == DORA_DTYPE_F16)
+    return launch_pdl(norm_finalize_gram_kernel<TO, __half>, grid, block, 0, st, wpart, nw, cpart, nc, gpart, ng, r,
+                      static_cast<const __half*>(B), M, two_s, s2, static_cast<TO*>(norm_out), parts);
+  return launch_pdl(norm_finalize_gram_kernel<TO, __nv_bfloat16>, grid, block, 0, st, wpart, nw, cpart, nc, gpart, ng,
+                    r, static_cast<const __nv_bfloat16*>(B), M, two_s, s2, static_cast<TO*>(norm_out), parts);
+}
+
+void launch_norm_finalize_gram(const float* wpart, int nw, const float* cpart, int nc, const float* gpart, int ng,
+                               int r, const void* B, int b_dtype, int64_t M, double scale, int out_dtype,
+                               void* norm_out, float* parts, cudaStream_t st) {
+  const float two_s = float(2.0 * scale), s2 = float(scale * scale);
+  cudaError_t e;
+  switch (out_dtype) {
+    case DORA_DTYPE_F16:
+      e = launch_finalize_gram_t<__half>(wpart, nw, cpart, nc, gpart, ng, r, B, b_dtype, M, two_s, s2, norm_out,
+                                         parts, st);
+      break;
+    default:
+      e = launch_finalize_gram_t<__nv_bfloat16>(wpart, nw, cpart, nc, gpart, ng, r, B, b_dtype, M, two_s, s2,
+                                                norm_out, parts, st);
       break;
   }
   if (e != cudaSuccess) set_cuda_error(e);

@@ -57,7 +57,17 @@ struct SkArgs {
   float* rowdot_part;  // [slots * n_tiles][M], entry (slot * n_tiles + n_tile)
   float* sumsq_part;   // [slots][M] (from the n_tile = 0 tiles)
   float* v_part;       // [slots][M] when fuse_v
+  // Low-rank Gram (nt == 16, no fused B G B^T): every CTA writes its partial
+  // G = sum A_k A_k^T over the k-blocks it is responsible for, [grid][16 x 16].
+  int fuse_g, kb_total;
+  float* g_part;
 };
+
+// The tile whose CTA adds k-block kb of A to its partial Gram: k-blocks are spread
+// evenly over the tiles, so every CTA gets about the same share.
+__host__ __device__ inline int64_t gram_tile(int64_t kb, int64_t kb_total, int64_t m_tiles) {
+  return kb * m_tiles / kb_total;
+}
 
 __host__ __device__ inline uint32_t sk_stage_bytes(int nt) { return kXTileBytes + uint32_t(nt) * 128u; }
 
@@ -357,6 +367,10 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
     int64_t gk = 0;
     int n_done = 0, n_vdone = 0;
     int seg = 0;
+    // Partial Gram entries of this thread: G[ga][gb] and G[ga][gb + 1] (nt == 16:
+    // 128 row threads x 2 = all 256 entries).
+    const int ga = row >> 3, gb = (row & 7) * 2;
+    float g0 = 0.f, g1 = 0.f;
     for (int64_t u = u_first; u < u_last; ++seg) {
       const Seg sg = segment(u);
       u = sg.tile * TU + sg.ub;
@@ -388,6 +402,30 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
               for (int e = 0; e < 8; ++e) {
                 const float x = to_f32(h[e]);
                 ssq8[e] = fmaf(x, x, ssq8[e]);
+              }
+            }
+            if (a.fuse_g) {
+              // This k-block's A rows are staged right after its X tile (16 rows of
+              // 128 bytes, 128-byte swizzle: chunk c of row q at c ^ (q & 7)).
+              const int64_t kb = int64_t(sg.ua + i) * ksub + hb;
+              if (kb < a.kb_total && gram_tile(kb, a.kb_total, a.m_tiles) == sg.m_tile) {
+                const uint8_t* ay = base + size_t(s) * stage_bytes + size_t(hb) * sub_bytes + kXTileBytes;
+#pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                  const uint4 va = *reinterpret_cast<const uint4*>(ay + ga * 128 + ((p ^ (ga & 7)) * 16));
+                  const uint4 vb0 = *reinterpret_cast<const uint4*>(ay + gb * 128 + ((p ^ (gb & 7)) * 16));
+                  const uint4 vb1 =
+                      *reinterpret_cast<const uint4*>(ay + (gb + 1) * 128 + ((p ^ ((gb + 1) & 7)) * 16));
+                  const T* xa = reinterpret_cast<const T*>(&va);
+                  const T* x0 = reinterpret_cast<const T*>(&vb0);
+                  const T* x1 = reinterpret_cast<const T*>(&vb1);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) {
+                    const float av = to_f32(xa[e]);
+                    g0 = fmaf(av, to_f32(x0[e]), g0);
+                    g1 = fmaf(av, to_f32(x1[e]), g1);
+                  }
+                }
               }
             }
           }
@@ -440,6 +478,12 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(seg_free);
     }
+    if (a.fuse_g) {
+      // Every CTA writes its slot (zeros when it had no Gram k-blocks), so the
+      // finalize sums a fixed number of partials in a fixed order.
+      a.g_part[c * 256 + ga * 16 + gb] = g0;
+      a.g_part[c * 256 + ga * 16 + gb + 1] = g1;
+    }
   }
 
   tc_fence_before();
@@ -491,7 +535,7 @@ SkPlan tc_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
 }
 
 template <typename T, bool SSQ>
-static int launch_sk(const tc::SkArgs& k, const CUtensorMap* m, cudaStream_t st) {
+static int launch_sk(const tc::SkArgs& k, const CUtensorMap* m, cudaStream_t st, bool pdl) {
   const uint32_t smem = 1024u + k.bar_off + 512u;
   auto kfn = tc::tc_sk_rowdot_kernel<T, SSQ>;
   static std::atomic<unsigned long long> opted{0};
@@ -505,8 +549,15 @@ static int launch_sk(const tc::SkArgs& k, const CUtensorMap* m, cudaStream_t st)
     opted.fetch_or(bit, std::memory_order_relaxed);
   }
   // Launched as a programmatic dependent of the Gram reduce: the X Y^T units start at
-  // once, the producer waits for the reduce only before its first G load.
-  e = launch_pdl(kfn, dim3(unsigned(k.grid)), dim3(tc::kThreads), smem, st, m[0], m[1], m[2], m[3], m[4], k);
+  // once, the producer waits for the reduce only before its first G load.  With the
+  // Gram fused in (low rank) it is the chain's first kernel: an ordinary launch, which
+  // waits for whatever wrote W0, A and B before it.
+  if (pdl)
+    e = launch_pdl(kfn, dim3(unsigned(k.grid)), dim3(tc::kThreads), smem, st, m[0], m[1], m[2], m[3], m[4], k);
+  else {
+    kfn<<<dim3(unsigned(k.grid)), dim3(tc::kThreads), smem, st>>>(m[0], m[1], m[2], m[3], m[4], k);
+    e = cudaSuccess;
+  }
   if (e != cudaSuccess) return set_cuda_error(e);
   return check_launch();
 }
@@ -552,8 +603,12 @@ int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.rowdot_part = a.rowdot_part;
   k.sumsq_part = a.sumsq_part;
   k.v_part = a.v_part;
-  if (a.dtype == DORA_DTYPE_BF16) return launch_sk<__nv_bfloat16, true>(k, maps, st);
-  return launch_sk<__half, true>(k, maps, st);
+  k.fuse_g = a.g_part ? 1 : 0;
+  k.kb_total = sh.kblocks;
+  k.g_part = a.g_part;
+  if (k.fuse_g && (fuse || sh.nt != 16 || ybox != 16)) return DORA_ERR_INVALID_ARGUMENT;
+  if (a.dtype == DORA_DTYPE_BF16) return launch_sk<__nv_bfloat16, true>(k, maps, st, !k.fuse_g);
+  return launch_sk<__half, true>(k, maps, st, !k.fuse_g);
 }
 
 }  // namespace dora

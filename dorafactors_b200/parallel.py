@@ -227,11 +227,15 @@ class _RowShardedDoraFn(torch.autograd.Function):
             needs_m = m.requires_grad
             inner = torch.empty_like(lora) if needs_m else None
             entry = layer.pool.acquire(x2.shape[0], ld, lora.dtype, lora.device)
-            layer.pool.barrier(lora.device)  # every rank is done reading its buffer
             bvec = None if bias is None else bias.detach().to(lora.dtype).contiguous()
-            _native.linear_output_fwd_allgather(lora, result, bvec, gk.contiguous(), s, entry["ptrs"], rank, col0,
-                                                ld, inner)
-            layer.pool.barrier(lora.device)  # every rank's columns have landed in every buffer
+            if world == 1:
+                # One shard holds every column: nothing to gather.
+                _native.linear_output_fwd(lora, result, bvec, gk.contiguous(), s, entry["buf"], inner)
+            else:
+                layer.pool.barrier(lora.device)  # every rank is done reading its buffer
+                _native.linear_output_fwd_allgather(lora, result, bvec, gk.contiguous(), s, entry["ptrs"], rank,
+                                                    col0, ld, inner)
+                layer.pool.barrier(lora.device)  # every rank's columns have landed in every buffer
             y = entry["buf"].view(*x.shape[:-1], ld)
         ctx.layer, ctx.col0, ctx.world, ctx.x_shape = layer, col0, world, x.shape
         ctx.m_dtype = m.dtype

@@ -91,6 +91,9 @@ CASES = [
     (700, 2048, 200, "bf16"),  # two k-blocks per stream-K stage, two stages
     (300, 1000, 176, "fp16"),  # the same with a ragged last unit (16 k-blocks, K % 64 != 0)
     (700, 4160, 256, "bf16"),  # CTA-pair stream-K, two k-blocks per stage, 65 k-blocks (last stage half past K)
+    (3000, 4104, 16, "bf16"),  # low rank: Gram fused into the stream-K kernel, ragged K and M
+    (1000, 2048, 8, "fp16"),  # the same in fp16, r = 8 (A's box reads zero rows past r)
+    (100, 8192, 16, "bf16"),  # one partial tile: every Gram k-block on the same tile
 ]
 
 
@@ -188,7 +191,8 @@ def _torch_fp32_norm_parts(W, A, B):
     return w, c, b
 
 
-@pytest.mark.parametrize("out_f,in_f,r", [(28672, 8192, 384), (8192, 8192, 1024), (8192, 8192, 16)])
+@pytest.mark.parametrize("out_f,in_f,r", [(28672, 8192, 384), (8192, 8192, 1024), (8192, 8192, 16),
+                                         (28672, 8192, 16), (28672, 8192, 8)])
 def test_norm_full_size_vs_torch_fp32(out_f, in_f, r):
     """Layer sizes of the benchmark: the tcgen05 result against PyTorch fp32 GEMMs on the same GPU."""
     from dorafactors_b200 import _native
