@@ -370,7 +370,15 @@ def run_native(args) -> None:
     sweep = None
     if not args.no_extras and world == 1:
         timer.enabled = False
+        # The sweep times single calls of a few tens of microseconds: after the
+        # power-capped GEMM-heavy steps above, one idle second lets the SM clock
+        # return from its capped state, and the clocks seen during the sweep are
+        # reported with it.
+        time.sleep(1.0)
+        sweep_clocks = ClockSampler(physical_gpu_index(local_rank))
+        sweep_clocks.start()
         sweep = measure_rank_sweep(device)
+        sweep["clocks"] = sweep_clocks.stop()
     model = None
     if not args.no_extras and world == MODEL_EXTRA_WORLD:
         timer.enabled = False

@@ -80,6 +80,15 @@ static int sk2_mode() {
   return mode;
 }
 
+// DORA_B200_FUSE_G=0 keeps the separate Gram launches at r <= 16.
+static bool use_fused_gram() {
+  static const bool on = [] {
+    const char* e = std::getenv("DORA_B200_FUSE_G");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // DORA_B200_SK=0 selects the split-K cross-term kernel instead of the stream-K one.
 static bool use_sk_kernel() {
   static const bool on = [] {
@@ -127,7 +136,7 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
   // up the Gram matrix from the A tiles they already hold, and the finalize forms
   // B G B^T on CUDA cores (256 FMAs per row), so the Gram, its reduce and the
   // B G B^T units leave the launch sequence.
-  p.fuse_g = p.tc_u && r <= 16 && r % 8 == 0 && use_sk_kernel() && !use_pair_kernel() && sk2_mode() != 1;
+  p.fuse_g = p.tc_u && r <= 16 && r % 8 == 0 && use_fused_gram() && use_sk_kernel() && !use_pair_kernel() && sk2_mode() != 1;
   if (p.fuse_g) p.fuse_v = false;
   if (p.tc_u) {
     const TcGemmShape u = tc_gemm_shape(out, r, in);

@@ -229,22 +229,35 @@ __global__ void __launch_bounds__(256) norm_finalize_gram_kernel(
     const float* __restrict__ gpart, int ng, int r, const TB* __restrict__ B, int64_t M, float two_s, float s2,
     TO* __restrict__ norm_out, float* __restrict__ parts) {
   __shared__ float G[16][17];
+  const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool live = m < M;
+  // B is an input of the layer, not of the previous kernel: read before the wait.
+  float bj[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) bj[k] = (live && k < r) ? to_f32(B[m * r + k]) : 0.f;
   pdl_wait();  // the partials come from the previous kernel
   {
-    const int e = threadIdx.x;  // 256 threads, one Gram entry each
+    // 256 threads, one Gram entry each, summed in CTA order; sixteen loads are
+    // issued before their additions so the partials' L2 latency is paid ng / 16
+    // times instead of ng times.
+    const int e = threadIdx.x;
     float t = 0.f;
-    for (int i = 0; i < ng; ++i) t += gpart[int64_t(i) * 256 + e];
+    int i = 0;
+    for (; i + 16 <= ng; i += 16) {
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = gpart[int64_t(i + j) * 256 + e];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) t += v[j];
+    }
+    for (; i < ng; ++i) t += gpart[int64_t(i) * 256 + e];
     G[e >> 4][e & 15] = t;
   }
   __syncthreads();
-  const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (m >= M) return;
+  if (!live) return;
   float w = 0.f, c = 0.f;
   for (int i = 0; i < nw; ++i) w += wpart[int64_t(i) * M + m];
   for (int i = 0; i < nc; ++i) c += cpart[int64_t(i) * M + m];
-  float bj[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) bj[k] = k < r ? to_f32(B[m * r + k]) : 0.f;
   float b = 0.f;
 #pragma unroll
   for (int x = 0; x < 16; ++x) {

@@ -377,6 +377,12 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       const int64_t m = sg.m_tile * BM + row;
       cur_n0 = sg.n_tile * nt;
       const bool ssq_tile = sg.n_tile == 0;  // ||X||^2 once per row block
+      // k-blocks [kg_lo, kg_hi) of A go into this tile's partial Gram (gram_tile(kb) == m_tile).
+      int kg_lo = 0, kg_hi = 0;
+      if (a.fuse_g) {
+        kg_lo = int((sg.m_tile * a.kb_total + a.m_tiles - 1) / a.m_tiles);
+        kg_hi = int(((sg.m_tile + 1) * a.kb_total + a.m_tiles - 1) / a.m_tiles);
+      }
       float ssq8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight independent FMA chains
       bool ok = true;
       if (kSumSq) {
@@ -397,18 +403,13 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
             for (int p = 0; p < 8; ++p) {
               // Rotate the 16-byte chunk order by lane so a quarter-warp touches 8 distinct bank groups.
               const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((p + lane) & 7) * 16);
-              const T* h = reinterpret_cast<const T*>(&v);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float x = to_f32(h[e]);
-                ssq8[e] = fmaf(x, x, ssq8[e]);
-              }
+              sumsq8<T>(v, ssq8);
             }
-            if (a.fuse_g) {
+            {
               // This k-block's A rows are staged right after its X tile (16 rows of
               // 128 bytes, 128-byte swizzle: chunk c of row q at c ^ (q & 7)).
-              const int64_t kb = int64_t(sg.ua + i) * ksub + hb;
-              if (kb < a.kb_total && gram_tile(kb, a.kb_total, a.m_tiles) == sg.m_tile) {
+              const int kb = (sg.ua + i) * ksub + hb;
+              if (kb >= kg_lo && kb < kg_hi) {
                 const uint8_t* ay = base + size_t(s) * stage_bytes + size_t(hb) * sub_bytes + kXTileBytes;
 #pragma unroll
                 for (int p = 0; p < 8; ++p) {

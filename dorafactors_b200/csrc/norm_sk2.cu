@@ -351,12 +351,7 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
             const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((p + lane) & 7) * 16);
-            const T* h = reinterpret_cast<const T*>(&v);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float x = to_f32(h[e]);
-              ssq8[e] = fmaf(x, x, ssq8[e]);
-            }
+            sumsq8<T>(v, ssq8);
           }
         }
         __syncwarp();

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <mutex>
+#include <type_traits>
 
 #include "norm_internal.cuh"
 
@@ -67,6 +68,28 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   ok = __shfl_sync(0xffffffffu, ok, 0);
   __syncwarp();
   return ok;
+}
+
+// Row sums of squares: acc[e] += x_e * x_e for the eight half-precision values in v,
+// one mixed-precision FMA (half inputs, fp32 addend and result) per element.  Half
+// values are exact in fp32, so each step equals fmaf(float(x), float(x), acc[e]) bit
+// for bit, without a conversion instruction per element.
+template <typename T>
+__device__ __forceinline__ void sumsq8(const uint4& v, float* acc) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+      asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+          "fma.rn.f32.bf16 %0, l, l, %0;\n\tfma.rn.f32.bf16 %1, h, h, %1;\n\t}"
+          : "+f"(acc[2 * j]), "+f"(acc[2 * j + 1])
+          : "r"(w[j]));
+    else
+      asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+          "fma.rn.f32.f16 %0, l, l, %0;\n\tfma.rn.f32.f16 %1, h, h, %1;\n\t}"
+          : "+f"(acc[2 * j]), "+f"(acc[2 * j + 1])
+          : "r"(w[j]));
+  }
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
