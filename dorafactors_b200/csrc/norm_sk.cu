@@ -61,6 +61,10 @@ struct SkArgs {
   // G = sum A_k A_k^T over the k-blocks it is responsible for, [grid][16 x 16].
   int fuse_g, kb_total;
   float* g_part;
+  // With fuse_g the row threads read their B row (nt = 16 values) from here into
+  // registers at each segment start instead of staging the B tile: the ring never
+  // drains between segments.
+  const void* zsrc;
 };
 
 // The tile whose CTA adds k-block kb of A to its partial Gram: k-blocks are spread
@@ -229,7 +233,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
         const int n0 = sg.n_tile * nt;
         // Ring mode: the previous segment's epilogues must be done with the staged Z / G
         // (which live in the ring) before the ring is refilled.
-        if (!a.apart && seg > 0 && !mbar_wait(seg_free, (seg - 1) & 1)) { *aborted = 1; break; }
+        if (!a.fuse_g && !a.apart && seg > 0 && !mbar_wait(seg_free, (seg - 1) & 1)) { *aborted = 1; break; }
         for (int i = 0; i < sg.u_iters; ++i) {
           const int64_t g = gk;
           const int s = int(g % S);
@@ -251,6 +255,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
             for (int j = 0; j < nzb; ++j) tma_prefetch_2d(&tmZ, n0 + j * BK, m0);
         }
         if (*aborted) break;
+        if (a.fuse_g) continue;  // no B tile to stage: the next segment's loads follow at once
         bool ok = true;
         if (a.apart) {
           // Own region: only the previous segment's epilogues have to be done with it.
@@ -376,6 +381,13 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       u = sg.tile * TU + sg.ub;
       const int64_t m = sg.m_tile * BM + row;
       cur_n0 = sg.n_tile * nt;
+      // fuse_g: this row's N (8 or 16) B values; rows are N * 2 bytes, 16-byte aligned.
+      uint4 zr0 = make_uint4(0u, 0u, 0u, 0u), zr1 = zr0;
+      if (a.fuse_g && m < a.M) {
+        const uint4* zp = reinterpret_cast<const uint4*>(static_cast<const T*>(a.zsrc) + m * a.N);
+        zr0 = __ldg(zp);
+        if (a.N > 8) zr1 = __ldg(zp + 1);
+      }
       const bool ssq_tile = sg.n_tile == 0;  // ||X||^2 once per row block
       // k-blocks [kg_lo, kg_hi) of A go into this tile's partial Gram (gram_tile(kb) == m_tile).
       int kg_lo = 0, kg_hi = 0;
@@ -436,7 +448,7 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       }
       const int64_t first = sk_owner(sg.tile * TU, TOT, G);
       const int slot = int(c - first);
-      ok = ok && __all_sync(0xffffffffu, !*aborted && mbar_wait(zfull, seg & 1) &&
+      ok = ok && __all_sync(0xffffffffu, !*aborted && (a.fuse_g || mbar_wait(zfull, seg & 1)) &&
                                              (sg.u_iters == 0 || mbar_wait(done, n_done & 1)));
       if (!ok) {
         *aborted = 1;
@@ -444,7 +456,26 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
       }
       if (sg.u_iters > 0) ++n_done;
       tc_fence_after();
-      const float cacc = sg.u_iters > 0 ? rowdot_epilogue() : 0.f;
+      float cacc = 0.f;
+      if (a.fuse_g) {
+        // 16 accumulator columns; TMEM goes back to the MMA warp as soon as it is read,
+        // so the next segment's MMAs overlap this dot (same order as dot_staged).
+        float v[32];
+        tmem_ld32(trow, v);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(seg_free);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const T* z0 = reinterpret_cast<const T*>(&zr0);
+        const T* z1 = reinterpret_cast<const T*>(&zr1);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(v[e], to_f32(z0[e]), acc[e]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(v[8 + e], to_f32(z1[e]), acc[e]);
+        cacc = sum8(acc);
+      } else if (sg.u_iters > 0) {
+        cacc = rowdot_epilogue();
+      }
       if (m < a.M) {
         a.rowdot_part[(int64_t(slot) * a.n_tiles + sg.n_tile) * a.M + m] = cacc;
         if (ssq_tile) a.sumsq_part[int64_t(slot) * a.M + m] = sum8(ssq8);
@@ -475,9 +506,11 @@ tc_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_consta
           if (a.fuse_v) a.v_part[int64_t(s2) * a.M + m] = 0.f;
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(seg_free);
+      if (!a.fuse_g) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(seg_free);
+      }
     }
     if (a.fuse_g) {
       // Every CTA writes its slot (zeros when it had no Gram k-blocks), so the
@@ -607,6 +640,7 @@ int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.fuse_g = a.g_part ? 1 : 0;
   k.kb_total = sh.kblocks;
   k.g_part = a.g_part;
+  k.zsrc = a.Z;
   if (k.fuse_g && (fuse || sh.nt != 16 || ybox != 16)) return DORA_ERR_INVALID_ARGUMENT;
   if (a.dtype == DORA_DTYPE_BF16) return launch_sk<__nv_bfloat16, true>(k, maps, st, !k.fuse_g);
   return launch_sk<__half, true>(k, maps, st, !k.fuse_g);

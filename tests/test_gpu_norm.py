@@ -94,6 +94,8 @@ CASES = [
     (3000, 4104, 16, "bf16"),  # low rank: Gram fused into the stream-K kernel, ragged K and M
     (1000, 2048, 8, "fp16"),  # the same in fp16, r = 8 (A's box reads zero rows past r)
     (100, 8192, 16, "bf16"),  # one partial tile: every Gram k-block on the same tile
+    (20000, 512, 16, "bf16"),  # low rank, short K: two to three segments per CTA back to back
+    (5000, 256, 8, "bf16"),  # one unit per tile: every unit its own segment
 ]
 
 
