@@ -237,18 +237,19 @@ __global__ void __launch_bounds__(256) norm_finalize_gram_kernel(
   for (int k = 0; k < 16; ++k) bj[k] = (live && k < r) ? to_f32(B[m * r + k]) : 0.f;
   pdl_wait();  // the partials come from the previous kernel
   {
-    // 256 threads, one Gram entry each, summed in CTA order; sixteen loads are
-    // issued before their additions so the partials' L2 latency is paid ng / 16
-    // times instead of ng times.
+    // 256 threads, one Gram entry each, summed in CTA order; 32 loads are issued
+    // before their additions so the partials' L2 latency is paid ng / 32 times
+    // instead of ng times (this sum is on the call's critical path, after the
+    // stream-K kernel).
     const int e = threadIdx.x;
     float t = 0.f;
     int i = 0;
-    for (; i + 16 <= ng; i += 16) {
-      float v[16];
+    for (; i + 32 <= ng; i += 32) {
+      float v[32];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = gpart[int64_t(i + j) * 256 + e];
+      for (int j = 0; j < 32; ++j) v[j] = gpart[int64_t(i + j) * 256 + e];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) t += v[j];
+      for (int j = 0; j < 32; ++j) t += v[j];
     }
     for (; i < ng; ++i) t += gpart[int64_t(i) * 256 + e];
     G[e >> 4][e & 15] = t;
