@@ -231,34 +231,45 @@ __global__ void __launch_bounds__(256) norm_finalize_gram_kernel(
   __shared__ float G[16][17];
   const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const bool live = m < M;
-  // B is an input of the layer, not of the previous kernel: read before the wait.
+  // B is an input of the layer, not of the previous kernel: read before the wait
+  // (r is 8 or 16, rows of r * 2 bytes on 16-byte boundaries).
   float bj[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) bj[k] = (live && k < r) ? to_f32(B[m * r + k]) : 0.f;
-  pdl_wait();  // the partials come from the previous kernel
   {
-    // 256 threads, one Gram entry each, summed in CTA order; 32 loads are issued
-    // before their additions so the partials' L2 latency is paid ng / 32 times
-    // instead of ng times (this sum is on the call's critical path, after the
-    // stream-K kernel).
+    uint4 q[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+    if (live) {
+      const uint4* bp = reinterpret_cast<const uint4*>(B + m * r);
+      q[0] = __ldg(bp);
+      if (r > 8) q[1] = __ldg(bp + 1);
+    }
+    const TB* h = reinterpret_cast<const TB*>(q);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) bj[k] = k < r ? to_f32(h[k]) : 0.f;
+  }
+  pdl_wait();  // the partials come from the previous kernel
+  // This row's slot partials, issued before the Gram sum so their latency overlaps it.
+  float w = 0.f, c = 0.f;
+  if (live) {
+    for (int i = 0; i < nw; ++i) w += wpart[int64_t(i) * M + m];
+    for (int i = 0; i < nc; ++i) c += cpart[int64_t(i) * M + m];
+  }
+  {
+    // 256 threads, one Gram entry each, summed in CTA order.  Up to 64 loads are in
+    // flight before their additions, so the partials' latency is paid ng / 64 times:
+    // this sum is on the call's critical path, after the stream-K kernel.
     const int e = threadIdx.x;
     float t = 0.f;
-    int i = 0;
-    for (; i + 32 <= ng; i += 32) {
-      float v[32];
+    for (int i = 0; i < ng; i += 64) {
+      float v[64];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gpart[int64_t(i + j) * 256 + e];
+      for (int j = 0; j < 64; ++j) v[j] = i + j < ng ? gpart[int64_t(i + j) * 256 + e] : 0.f;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) t += v[j];
+      for (int j = 0; j < 64; ++j)
+        if (i + j < ng) t += v[j];
     }
-    for (; i < ng; ++i) t += gpart[int64_t(i) * 256 + e];
     G[e >> 4][e & 15] = t;
   }
   __syncthreads();
   if (!live) return;
-  float w = 0.f, c = 0.f;
-  for (int i = 0; i < nw; ++i) w += wpart[int64_t(i) * M + m];
-  for (int i = 0; i < nc; ++i) c += cpart[int64_t(i) * M + m];
   float b = 0.f;
 #pragma unroll
   for (int x = 0; x < 16; ++x) {
