@@ -199,10 +199,22 @@ __global__ void norm_finalize_kernel(const float* __restrict__ wpart, int nw, co
   pdl_wait();  // the partials come from the previous kernel
   const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (m >= M) return;
-  float w = 0.f, c = 0.f, b = 0.f;
-  for (int i = 0; i < nw; ++i) w += wpart[int64_t(i) * M + m];
-  for (int i = 0; i < nc; ++i) c += cpart[int64_t(i) * M + m];
-  for (int i = 0; i < nb; ++i) b += bpart[int64_t(i) * M + m];
+  // The partials are loaded eight at a time before they are added (in slot order),
+  // so this kernel, which runs after the stream-K kernel on the call's critical
+  // path, pays about one load latency instead of one per slot.
+  auto slot_sum = [&](const float* __restrict__ part, int n) {
+    float t = 0.f;
+    for (int i = 0; i < n; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = i + j < n ? part[int64_t(i + j) * M + m] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (i + j < n) t += v[j];
+    }
+    return t;
+  };
+  const float w = slot_sum(wpart, nw), c = slot_sum(cpart, nc), b = slot_sum(bpart, nb);
   float n;
   if (scale_zero) {
     const float x = (w > 0.f) ? w : ((w != w) ? w : 0.f);
