@@ -155,10 +155,17 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     }
     p.pair_u = use_pair_kernel() && tc2_supported(probe);
     const int m2 = sk2_mode();
+    const TcGemmShape u2 = tc2_sk_shape(out, r, in);
+    if (p.fuse_v && u2.n_tiles > 1 && !p.pair_u && use_sk_kernel() && (m2 == 1 || (m2 < 0 && u.nt >= 256))) {
+      // The pair kernel with several N tiles has no fused B G B^T phase.
+      p.fuse_v = false;
+      probe.G1 = probe.G2 = nullptr;
+      probe.v_part = nullptr;
+    }
     p.sk2_u = !p.pair_u && use_sk_kernel() && (m2 == 1 || (m2 < 0 && u.nt >= 256)) && tc2_sk_supported(probe);
     p.sk_u = !p.pair_u && !p.sk2_u && use_sk_kernel() && tc_sk_supported(probe);
     if (p.fuse_g && !p.sk_u) p.fuse_g = false;  // the single-CTA stream-K kernel carries the Gram
-    p.u_ntiles = u.n_tiles;
+    p.u_ntiles = p.sk2_u ? u2.n_tiles : u.n_tiles;
     if (p.sk2_u) {
       p.sk = tc2_sk_plan(out, r, in, p.fuse_v, sms);
       p.u_splits = p.sk.slots;

@@ -89,6 +89,9 @@ int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st);
 
 // Stream-K row-dot kernel on CTA pairs (norm_sk2.cu): the same contract over
 // 256-row pair tiles (M >= 256); SkPlan.grid counts clusters of two CTAs.
+// N tiling of the CTA-pair stream-K kernel (the N tile is the whole row up to 512
+// columns unless overridden for comparison, 256 columns above).
+TcGemmShape tc2_sk_shape(int64_t M, int64_t N, int64_t K);
 bool tc2_sk_supported(const TcGemmArgs& a);
 SkPlan tc2_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms);
 int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st);

@@ -19,6 +19,7 @@
 // TMA load reads this GPU's global memory into the issuing CTA's own shared
 // memory (the cta_group::2 form only signals the leader's barrier).
 #include <atomic>
+#include <cstdlib>
 #include <type_traits>
 
 #include "tc_common.cuh"
@@ -38,14 +39,15 @@ __host__ __device__ inline int64_t sk2_owner(int64_t x, int64_t total, int64_t g
 struct Sk2Args {
   int64_t M, N;
   int nt, pair_tiles, kblocks, stages, clusters, slots;
+  int n_tiles;  // N tiles of nt columns (r > 512; then no fused B G B^T phase)
   int ksub;  // 64-deep k-blocks per unit (one ring stage); kblocks counts units
   int apart;
   uint32_t stage_off, bar_off;
   int fuse_v, v_kblocks;
   int64_t units_per_tile, total_units;
   uint32_t tmem_cols;
-  float* rowdot_part;  // [slots][M]
-  float* sumsq_part;   // [slots][M]
+  float* rowdot_part;  // [slots * n_tiles][M], entry (slot * n_tiles + n_tile)
+  float* sumsq_part;   // [slots][M] (from the n_tile = 0 tiles)
   float* v_part;       // [slots][M] when fuse_v
 };
 
@@ -167,12 +169,16 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
 
   const int64_t u_first = sk2_begin(cl, TOT, G), u_last = sk2_begin(cl + 1, TOT, G);
   struct Seg {
-    int64_t tile;
-    int ua, ub, u_iters, v0, v_iters;
+    int64_t tile, m_pair;
+    int n_tile, ua, ub, u_iters, v0, v_iters;
   };
+  // Tiles run N-tile fastest: the N tiles of one pair of row blocks stream the same W0
+  // rows close together in time, so only the first reads them from DRAM.
   auto segment = [&](int64_t u) {
     Seg s;
     s.tile = u / TU;
+    s.m_pair = s.tile / a.n_tiles;
+    s.n_tile = int(s.tile % a.n_tiles);
     s.ua = int(u - s.tile * TU);
     const int64_t e = u_last - s.tile * TU;
     s.ub = int(e < TU ? e : TU);
@@ -195,7 +201,8 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
       for (int64_t u = u_first; u < u_last && !*aborted; ++seg) {
         const Seg sg = segment(u);
         u = sg.tile * TU + sg.ub;
-        const int m0 = int(sg.tile * 2 * BM + int64_t(rank) * BM);  // this CTA's rows
+        const int m0 = int(sg.m_pair * 2 * BM + int64_t(rank) * BM);  // this CTA's rows
+        const int n0 = sg.n_tile * nt;  // first column of the N tile (row of A / Z column)
         if (!a.apart && seg > 0 && !mbar_wait(seg_free, (seg - 1) & 1)) { *aborted = 1; break; }
         for (int i = 0; i < sg.u_iters; ++i) {
           const int64_t g = gk;
@@ -209,11 +216,11 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
             const int kx = ((sg.ua + i) * ksub + h) * BK;
             uint8_t* sX = stage + size_t(h) * sub_bytes;
             tma_load_2d_pair(sX, &tmX, bar_c, kx, m0);
-            tma_load_2d_pair(sX + kXTileBytes, &tmY, bar_c, kx, int(rank) * half_rows);
+            tma_load_2d_pair(sX + kXTileBytes, &tmY, bar_c, kx, n0 + int(rank) * half_rows);
           }
           ++gk;
           if (i == (sg.u_iters > S + 1 ? sg.u_iters - S - 1 : 0))
-            for (int j = 0; j < nzb; ++j) tma_prefetch_2d(&tmZ, j * BK, m0);
+            for (int j = 0; j < nzb; ++j) tma_prefetch_2d(&tmZ, n0 + j * BK, m0);
         }
         if (*aborted) break;
         bool ok = true;
@@ -224,7 +231,7 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
         }
         if (!ok) { *aborted = 1; break; }
         mbar_expect_tx(zfull, z_bytes);
-        for (int j = 0; j < nzb; ++j) tma_load_2d(zbase + size_t(j) * kXTileBytes, &tmZ, zfull, j * BK, m0);
+        for (int j = 0; j < nzb; ++j) tma_load_2d(zbase + size_t(j) * kXTileBytes, &tmZ, zfull, n0 + j * BK, m0);
         // Report the staged Z rows to the leader before loading G: the leader's Z G^T
         // MMAs need both CTAs' rows before they can release the G slots waited on below.
         if (!mbar_wait(zfull, seg & 1)) { *aborted = 1; break; }
@@ -311,9 +318,10 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
     const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16);
     const uint32_t leader_tmem_free = map_to_rank(tmem_free, 0);
     const uint32_t leader_tm_free = map_to_rank(tm_free, 0);
+    int cur_n0 = 0;  // first column of the current segment's N tile
     auto rowdot_epilogue = [&]() -> float {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      const int64_t ncols = a.N;
+      const int64_t ncols = a.N - cur_n0;
       int c0 = 0;
       for (; c0 + 64 <= int(a.tmem_cols) && c0 < nt; c0 += 64) {
         const int zc = pair_col_row(c0, nt);
@@ -339,14 +347,16 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
     for (int64_t u = u_first; u < u_last; ++seg) {
       const Seg sg = segment(u);
       u = sg.tile * TU + sg.ub;
-      const int64_t m = sg.tile * 2 * BM + int64_t(rank) * BM + row;
+      const int64_t m = sg.m_pair * 2 * BM + int64_t(rank) * BM + row;
+      cur_n0 = sg.n_tile * nt;
+      const bool ssq_tile = sg.n_tile == 0;  // ||W0||^2 once per row block
       float ssq8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // eight independent FMA chains
       bool ok = true;
       for (int i = 0; i < sg.u_iters; ++i) {
         const int64_t g = gk++;
         const int s = int(g % S);
         if (!warp_wait(&mdone[s], uint32_t((g / S) & 1))) { ok = false; break; }
-        for (int hb = 0; hb < ksub; ++hb) {
+        for (int hb = 0; ssq_tile && hb < ksub; ++hb) {
           const uint8_t* rowp = base + size_t(s) * stage_bytes + size_t(hb) * sub_bytes + row * 128;
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
@@ -369,8 +379,8 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
       tc_fence_after();
       const float cacc = sg.u_iters > 0 ? rowdot_epilogue() : 0.f;
       if (m < a.M) {
-        a.rowdot_part[int64_t(slot) * a.M + m] = cacc;
-        a.sumsq_part[int64_t(slot) * a.M + m] = sum8(ssq8);
+        a.rowdot_part[(int64_t(slot) * a.n_tiles + sg.n_tile) * a.M + m] = cacc;
+        if (ssq_tile) a.sumsq_part[int64_t(slot) * a.M + m] = sum8(ssq8);
       }
       float bacc = 0.f;
       if (sg.v_iters > 0) {
@@ -391,8 +401,8 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
       if (slot == 0 && m < a.M) {
         const int used = int(sk2_owner(sg.tile * TU + TU - 1, TOT, G) - first) + 1;
         for (int s2 = used; s2 < a.slots; ++s2) {
-          a.rowdot_part[int64_t(s2) * a.M + m] = 0.f;
-          a.sumsq_part[int64_t(s2) * a.M + m] = 0.f;
+          a.rowdot_part[(int64_t(s2) * a.n_tiles + sg.n_tile) * a.M + m] = 0.f;
+          if (ssq_tile) a.sumsq_part[int64_t(s2) * a.M + m] = 0.f;
           if (a.fuse_v) a.v_part[int64_t(s2) * a.M + m] = 0.f;
         }
       }
@@ -422,12 +432,48 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
 
 }  // namespace tc
 
+// N-tile width of the CTA-pair stream-K kernel: the whole row (up to 512 columns) by
+// default, 256-column tiles above; DORA_B200_PAIR_NT=<multiple of 32, at most 256>
+// splits narrower rows into tiles of that width too (then B G B^T is its own launch).
+static int pair_nt_override() {
+  static const int nt = [] {
+    const char* e = std::getenv("DORA_B200_PAIR_NT");
+    const int v = e ? std::atoi(e) : 0;
+    return (v >= 32 && v <= 256 && v % 32 == 0) ? v : 0;
+  }();
+  return nt;
+}
+
+// DORA_B200_PAIR_WIDE=0 splits rows wider than 512 columns into 256-column N tiles
+// instead of the widest equal tiles (for comparison).
+static bool pair_wide_tiles() {
+  static const bool on = [] {
+    const char* e = std::getenv("DORA_B200_PAIR_WIDE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+TcGemmShape tc2_sk_shape(int64_t M, int64_t N, int64_t K) {
+  const int f = pair_nt_override();
+  if (f > 0 && N > f) return tc_gemm_shape(M, N, K, f);
+  if (N > 512 && pair_wide_tiles()) {
+    // As few N tiles as hold the row at 512 columns each, of equal width (multiples of
+    // 128): fewer, wider units per k-block.
+    const int64_t tiles = (N + 511) / 512;
+    const int64_t w = ((N + tiles - 1) / tiles + 127) / 128 * 128;
+    return tc_gemm_shape(M, N, K, int(w));
+  }
+  return tc_gemm_shape(M, N, K);
+}
+
 bool tc2_sk_supported(const TcGemmArgs& a) {
   if (a.mode != kGemmRowdot || !a.sumsq || a.Y2 || !a.Z || a.ldz != a.N || (a.ldz * 2) % 16 != 0 ||
       !aligned16(a.Z))
     return false;
-  const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K);
-  if (sh.n_tiles != 1 || a.M < 2 * tc::BM) return false;
+  const TcGemmShape sh = tc2_sk_shape(a.M, a.N, a.K);
+  if (a.M < 2 * tc::BM) return false;
+  if (sh.n_tiles != 1 && a.G1) return false;  // the fused B G B^T phase needs the whole row in one tile
   const tc::Sk2Layout L = tc::sk2_layout(sh.nt, a.G1 != nullptr);
   const uint32_t z_bytes = uint32_t((sh.nt + tc::BK - 1) / tc::BK) * tc::kXTileBytes;
   const uint32_t staging = z_bytes + (a.G1 ? uint32_t(tc::kVSlots) * uint32_t(sh.nt) * 64u : 0u);
@@ -437,18 +483,19 @@ bool tc2_sk_supported(const TcGemmArgs& a) {
 }
 
 SkPlan tc2_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
-  const TcGemmShape sh = tc_gemm_shape(M, N, K);
+  const TcGemmShape sh = tc2_sk_shape(M, N, K);
   SkPlan p;
   const int64_t pair_tiles = (M + 2 * tc::BM - 1) / (2 * tc::BM);
   const int ksub = tc::sk2_layout(sh.nt, fuse_v).ksub;
   p.units_per_tile = int64_t((sh.kblocks + ksub - 1) / ksub) + (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
-  p.total_units = pair_tiles * p.units_per_tile;
+  const int64_t tiles = pair_tiles * sh.n_tiles;
+  p.total_units = tiles * p.units_per_tile;
   int64_t g = p.total_units / 4;
   if (g > sms / 2) g = sms / 2;
   if (g < 1) g = 1;
   p.grid = int(g);  // clusters of two CTAs
   int slots = 1;
-  for (int64_t t = 0; t < pair_tiles; ++t) {
+  for (int64_t t = 0; t < tiles; ++t) {
     const int64_t f = tc::sk2_owner(t * p.units_per_tile, p.total_units, g);
     const int64_t l = tc::sk2_owner(t * p.units_per_tile + p.units_per_tile - 1, p.total_units, g);
     if (int(l - f + 1) > slots) slots = int(l - f + 1);
@@ -478,7 +525,7 @@ static int launch_sk2(const tc::Sk2Args& k, const CUtensorMap* m, uint32_t smem,
 
 int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   if (!tc2_sk_supported(a)) return DORA_ERR_UNSUPPORTED;
-  const TcGemmShape sh = tc_gemm_shape(a.M, a.N, a.K);
+  const TcGemmShape sh = tc2_sk_shape(a.M, a.N, a.K);
   const int hb = sh.nt / 2;  // one box of A (and G) rows per CTA half (nt <= 512)
   const bool fuse = a.G1 != nullptr;
   CUtensorMap maps[5];
@@ -507,7 +554,8 @@ int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.fuse_v = fuse ? 1 : 0;
   k.v_kblocks = int((a.N + tc::BK - 1) / tc::BK);
   k.units_per_tile = int64_t(k.kblocks) + (fuse ? 2 * k.v_kblocks : 0);
-  k.total_units = int64_t(k.pair_tiles) * k.units_per_tile;
+  k.n_tiles = sh.n_tiles;
+  k.total_units = int64_t(k.pair_tiles) * k.n_tiles * k.units_per_tile;
   if (k.units_per_tile != p.units_per_tile || k.total_units != p.total_units) return DORA_ERR_INVALID_ARGUMENT;
   uint32_t cols = 32;
   while (cols < uint32_t(sh.nt)) cols <<= 1;
