@@ -128,6 +128,13 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, timeout_s: float = 3.0) -> None:
+        """Block until nvidia-smi has printed its first sample (it takes a moment to
+        start), so that a short measured region still gets sampled."""
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout_s:
+            time.sleep(0.02)
+
     def stop(self) -> dict | None:
         if self.proc is None:
             return None
@@ -377,6 +384,7 @@ def run_native(args) -> None:
         time.sleep(1.0)
         sweep_clocks = ClockSampler(physical_gpu_index(local_rank))
         sweep_clocks.start()
+        sweep_clocks.wait_first()
         sweep = measure_rank_sweep(device)
         sweep["clocks"] = sweep_clocks.stop()
     model = None

@@ -223,7 +223,7 @@ from dorafactors_b200 import _native
 out = {}
 for out_f, in_f, r in ((28672, 8192, 384), (8192, 4096, 256), (1000, 2048, 384), (640, 1024, 64),
                       (8192, 8192, 16), (4096, 4096, 512), (257, 320, 40), (2048, 2048, 768), (640, 1024, 520),
-                      (3000, 4104, 200), (1500, 4160, 256)):
+                      (3000, 4104, 200), (1500, 4160, 256), (1024, 1024, 1024), (3000, 4104, 16)):
     g = torch.Generator(device="cuda").manual_seed(out_f + r)
     W = (torch.randn(out_f, in_f, device="cuda", generator=g) * 0.02).bfloat16()
     A = ((torch.rand(r, in_f, device="cuda", generator=g) * 2 - 1) / in_f**0.5).bfloat16()
@@ -238,14 +238,22 @@ json.dump(out, sys.stdout)
 """
 
 
+_SWITCHES = ("DORA_B200_SK", "DORA_B200_PAIR", "DORA_B200_SK2", "DORA_B200_PAIR_NT", "DORA_B200_PAIR_WIDE",
+             "DORA_B200_FUSE_G")
+
+
 @pytest.mark.parametrize("env", [{"DORA_B200_SK": "0"}, {"DORA_B200_PAIR": "1"}, {"DORA_B200_SK2": "1"},
-                                 {"DORA_B200_SK2": "0"}],
-                         ids=["split_k", "cta_pair", "cta_pair_stream_k", "single_stream_k"])
+                                 {"DORA_B200_SK2": "0"}, {"DORA_B200_PAIR_NT": "128"}, {"DORA_B200_PAIR_WIDE": "0"},
+                                 {"DORA_B200_FUSE_G": "0"}],
+                         ids=["split_k", "cta_pair", "cta_pair_stream_k", "single_stream_k", "pair_n_tiles_128",
+                              "pair_n_tiles_256", "separate_gram"])
 def test_cross_term_kernels_agree(env):
     """The tcgen05 cross-term kernels give the same fp32 terms: the default choice
     (CTA-pair stream-K for r > 240, single-CTA stream-K below) against the split-K
-    kernel (DORA_B200_SK=0), the CTA-pair split-K kernel (DORA_B200_PAIR=1) and each
-    stream-K kernel forced everywhere (DORA_B200_SK2=1 / 0), in child processes."""
+    kernel (DORA_B200_SK=0), the CTA-pair split-K kernel (DORA_B200_PAIR=1), each
+    stream-K kernel forced everywhere (DORA_B200_SK2=1 / 0), the CTA-pair stream-K
+    kernel on narrower N tiles (DORA_B200_PAIR_NT=128, DORA_B200_PAIR_WIDE=0) and the
+    separate Gram launches at r <= 16 (DORA_B200_FUSE_G=0), in child processes."""
     import json
     import os
     import subprocess
@@ -254,7 +262,7 @@ def test_cross_term_kernels_agree(env):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     runs = {}
     for name, extra in (("default", {}), ("other", env)):
-        e = {k: v for k, v in os.environ.items() if k not in ("DORA_B200_SK", "DORA_B200_PAIR", "DORA_B200_SK2")}
+        e = {k: v for k, v in os.environ.items() if k not in _SWITCHES}
         e.update(extra)
         res = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, root], env=e, capture_output=True, text=True,
                              timeout=300)
@@ -267,6 +275,9 @@ def test_cross_term_kernels_agree(env):
         s = np.asarray(ref, np.float64).reshape(3, -1)
         # Different K partitions sum the fp32 partials in different orders: agreement to
         # fp32 rounding (normwise 1e-5, the same bound as against PyTorch's fp32 GEMMs).
+        # At r <= 16 the fused path forms B G B^T from the fp32 Gram on CUDA cores, the
+        # separate launches from its two-term bf16 split (about 2^-16 relative): 1e-4 there.
         for i in range(3):
+            tol = 1e-4 if (i == 2 and "DORA_B200_FUSE_G" in env) else 1e-5
             rel = np.linalg.norm(p[i] - s[i]) / max(np.linalg.norm(s[i]), 1e-30)
-            assert rel <= 1e-5, (key, i, rel)
+            assert rel <= tol, (key, i, rel)
