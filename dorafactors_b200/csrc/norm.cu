@@ -32,9 +32,10 @@ struct NormPlan {
   bool cast_a, cast_b;  // fp32 adapters rounded into the (half) weight dtype first
   bool tc_u, tc_v, tc_g, fuse_v, pair_u, sk_u, sk2_u;
   bool fuse_g;  // r <= 16: Gram inside the stream-K kernel, B G B^T in the finalize
-  SkPlan sk;
+  bool v_pair;  // B G B^T on the CTA-pair stream-K kernel: one launch for G's hi half, one for lo
+  SkPlan sk, vsk;
   int gram_splits, u_splits, u_ntiles, v_splits, v_ntiles;
-  size_t off_a, off_bh, off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, off_g16, total;
+  size_t off_a, off_bh, off_gpart, off_yt, off_hi, off_lo, off_w, off_c, off_b, off_g16, off_vs, total;
 };
 
 static size_t up256(size_t x) { return (x + 255) / 256 * 256; }
@@ -189,9 +190,29 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
     p.v_ntiles = 1;
     p.v_splits = p.u_splits;
   } else if (p.tc_v) {
-    const TcGemmShape v = tc_gemm_shape(out, r, r);
-    p.v_ntiles = v.n_tiles;
-    p.v_splits = pick_splits(int64_t(v.m_tiles) * v.n_tiles, 2 * v.kblocks, sms, 4);
+    // Above r = 512 the CTA-pair stream-K kernel forms B (G_hi + G_lo) in one launch (G_lo
+    // as a second Y), X = Z = B, its ||B||^2 output to scratch (8192^2: r = 768 0.168 ->
+    // 0.158 ms, r = 1024 0.212 -> 0.186 ms); at r = 512 the split-K launch is faster
+    // (0.099-0.103 against 0.110 ms).
+    TcGemmArgs vp{};
+    vp.mode = kGemmRowdot;
+    vp.Z = reinterpret_cast<const void*>(uintptr_t(256));
+    vp.ldz = r;
+    vp.M = out;
+    vp.N = r;
+    vp.K = r;
+    vp.sumsq = true;
+    vp.Y1 = vp.Y2 = vp.Z;
+    p.v_pair = r > 512 && use_sk_kernel() && sk2_mode() != 0 && !use_pair_kernel() && tc2_sk_supported(vp);
+    if (p.v_pair) {
+      p.vsk = tc2_sk_plan(out, r, r, false, sms, true);
+      p.v_splits = p.vsk.slots;
+      p.v_ntiles = tc2_sk_shape(out, r, r).n_tiles;
+    } else {
+      const TcGemmShape v = tc_gemm_shape(out, r, r);
+      p.v_ntiles = v.n_tiles;
+      p.v_splits = pick_splits(int64_t(v.m_tiles) * v.n_tiles, 2 * v.kblocks, sms, 4);
+    }
   } else {
     p.v_ntiles = int((r + 63) / 64);
     p.v_splits = 1;
@@ -207,6 +228,7 @@ static NormPlan make_plan(int64_t out, int64_t in, int64_t r, int wdt, int adt, 
   p.off_c = o;     o += up256(size_t(p.u_splits) * p.u_ntiles * out * 4);
   p.off_b = o;     o += up256(size_t(p.v_splits) * p.v_ntiles * out * 4);
   p.off_g16 = o;   o += p.fuse_g ? up256(size_t(p.sk.grid) * 256 * 4) : 0;
+  p.off_vs = o;    o += p.v_pair ? up256(size_t(p.vsk.slots) * out * 4) : 0;
   p.total = o;
   return p;
 }
@@ -332,6 +354,18 @@ extern "C" int dora_weight_norm(const void* W, const void* A, const void* B, int
 
   // 4. B G B^T term (already done above when fused).
   if (p.fuse_v) {
+  } else if (p.v_pair) {
+    // An ordinary launch: it reads G's halves from the Gram reduce, which the stream-K
+    // cross-term kernel before it does not wait for, so it waits for everything before
+    // it; the finalize after it then sees every partial.
+    TcGemmArgs v{};
+    v.dtype = b_dtype; v.X = B; v.Y1 = hi; v.Y2 = lo; v.Z = B; v.ldz = R;
+    v.M = M; v.N = R; v.K = R; v.mode = kGemmRowdot; v.sumsq = true; v.k_splits = p.v_splits;
+    v.rowdot_part = bpart;
+    v.sumsq_part = reinterpret_cast<float*>(ws + p.off_vs);
+    v.plain_launch = true;
+    if (!tc2_sk_supported(v)) return DORA_ERR_INVALID_ARGUMENT;
+    if ((rc = tc2_sk_rowdot_gemm(v, p.vsk, st))) return rc;
   } else if (p.tc_v) {
     TcGemmArgs v{};
     v.dtype = b_dtype; v.X = B; v.Y1 = hi; v.Y2 = lo; v.Z = B; v.ldz = R;

@@ -54,6 +54,10 @@ struct TcGemmArgs {
   // Stream-K kernel, N tile of 16 without the fused B G B^T phase: also emit partial
   // Gram matrices A A^T, [grid][16 x 16] fp32 (one per CTA, fixed-order summable).
   float* g_part = nullptr;
+  // Launch as an ordinary stream-ordered kernel instead of a programmatic dependent of
+  // the previous launch (the kernel then needs no griddepcontrol.wait before reading
+  // what earlier kernels wrote).
+  bool plain_launch = false;
 };
 constexpr int kGramTile = 128;
 struct TcGemmShape {
@@ -89,11 +93,11 @@ int tc_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st);
 
 // Stream-K row-dot kernel on CTA pairs (norm_sk2.cu): the same contract over
 // 256-row pair tiles (M >= 256); SkPlan.grid counts clusters of two CTAs.
-// N tiling of the CTA-pair stream-K kernel (the N tile is the whole row up to 512
-// columns unless overridden for comparison, 256 columns above).
+// N tiling of the CTA-pair stream-K kernel: the whole row up to 512 columns, the
+// widest equal tiles of at most 512 columns above (unless overridden for comparison).
 TcGemmShape tc2_sk_shape(int64_t M, int64_t N, int64_t K);
 bool tc2_sk_supported(const TcGemmArgs& a);
-SkPlan tc2_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms);
+SkPlan tc2_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms, bool two_y = false);
 int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st);
 
 }  // namespace dora

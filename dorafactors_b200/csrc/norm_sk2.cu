@@ -40,6 +40,9 @@ struct Sk2Args {
   int64_t M, N;
   int nt, pair_tiles, kblocks, stages, clusters, slots;
   int n_tiles;  // N tiles of nt columns (r > 512; then no fused B G B^T phase)
+  // With a second Y (Y2 in the tmG2 slot, no fused phase): the first y2_units units of a
+  // tile multiply X by Y1, the next y2_units X (re-read) by Y2, into one accumulator.
+  int y2_units;
   int ksub;  // 64-deep k-blocks per unit (one ring stage); kblocks counts units
   int apart;
   uint32_t stage_off, bar_off;
@@ -212,11 +215,14 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
           uint8_t* stage = base + size_t(s) * stage_bytes;
           const uint32_t bar_c = map_to_rank(&full[s], 0);
           if (leader) mbar_expect_tx(&full[s], 2u * stage_bytes);
+          const int iu = sg.ua + i;
+          const bool second = a.y2_units > 0 && iu >= a.y2_units;
+          const int lu = second ? iu - a.y2_units : iu;
           for (int h = 0; h < ksub; ++h) {  // k-blocks past K read zeros and count in full
-            const int kx = ((sg.ua + i) * ksub + h) * BK;
+            const int kx = (lu * ksub + h) * BK;
             uint8_t* sX = stage + size_t(h) * sub_bytes;
             tma_load_2d_pair(sX, &tmX, bar_c, kx, m0);
-            tma_load_2d_pair(sX + kXTileBytes, &tmY, bar_c, kx, n0 + int(rank) * half_rows);
+            tma_load_2d_pair(sX + kXTileBytes, second ? &tmG2 : &tmY, bar_c, kx, n0 + int(rank) * half_rows);
           }
           ++gk;
           if (i == (sg.u_iters > S + 1 ? sg.u_iters - S - 1 : 0))
@@ -356,7 +362,8 @@ tc2_sk_rowdot_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_const
         const int64_t g = gk++;
         const int s = int(g % S);
         if (!warp_wait(&mdone[s], uint32_t((g / S) & 1))) { ok = false; break; }
-        for (int hb = 0; ssq_tile && hb < ksub; ++hb) {
+        const bool ssq_unit = ssq_tile && !(a.y2_units > 0 && sg.ua + i >= a.y2_units);  // X once
+        for (int hb = 0; ssq_unit && hb < ksub; ++hb) {
           const uint8_t* rowp = base + size_t(s) * stage_bytes + size_t(hb) * sub_bytes + row * 128;
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
@@ -468,9 +475,9 @@ TcGemmShape tc2_sk_shape(int64_t M, int64_t N, int64_t K) {
 }
 
 bool tc2_sk_supported(const TcGemmArgs& a) {
-  if (a.mode != kGemmRowdot || !a.sumsq || a.Y2 || !a.Z || a.ldz != a.N || (a.ldz * 2) % 16 != 0 ||
-      !aligned16(a.Z))
+  if (a.mode != kGemmRowdot || !a.sumsq || !a.Z || a.ldz != a.N || (a.ldz * 2) % 16 != 0 || !aligned16(a.Z))
     return false;
+  if (a.Y2 && a.G1) return false;  // a second Y shares the map slot of the fused phase's G
   const TcGemmShape sh = tc2_sk_shape(a.M, a.N, a.K);
   if (a.M < 2 * tc::BM) return false;
   if (sh.n_tiles != 1 && a.G1) return false;  // the fused B G B^T phase needs the whole row in one tile
@@ -482,12 +489,13 @@ bool tc2_sk_supported(const TcGemmArgs& a) {
   return true;
 }
 
-SkPlan tc2_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
+SkPlan tc2_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms, bool two_y) {
   const TcGemmShape sh = tc2_sk_shape(M, N, K);
   SkPlan p;
   const int64_t pair_tiles = (M + 2 * tc::BM - 1) / (2 * tc::BM);
   const int ksub = tc::sk2_layout(sh.nt, fuse_v).ksub;
-  p.units_per_tile = int64_t((sh.kblocks + ksub - 1) / ksub) + (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
+  p.units_per_tile = int64_t((sh.kblocks + ksub - 1) / ksub) * (two_y ? 2 : 1) +
+                     (fuse_v ? 2 * ((N + tc::BK - 1) / tc::BK) : 0);
   const int64_t tiles = pair_tiles * sh.n_tiles;
   p.total_units = tiles * p.units_per_tile;
   int64_t g = p.total_units / 4;
@@ -505,7 +513,7 @@ SkPlan tc2_sk_plan(int64_t M, int64_t N, int64_t K, bool fuse_v, int sms) {
 }
 
 template <typename T>
-static int launch_sk2(const tc::Sk2Args& k, const CUtensorMap* m, uint32_t smem, cudaStream_t st) {
+static int launch_sk2(const tc::Sk2Args& k, const CUtensorMap* m, uint32_t smem, cudaStream_t st, bool plain) {
   auto kfn = tc::tc2_sk_rowdot_kernel<T>;
   static std::atomic<unsigned long long> opted{0};
   int dev = 0;
@@ -517,8 +525,15 @@ static int launch_sk2(const tc::Sk2Args& k, const CUtensorMap* m, uint32_t smem,
     if (e != cudaSuccess) return set_cuda_error(e);
     opted.fetch_or(bit, std::memory_order_relaxed);
   }
-  // Programmatic dependent of the Gram reduce (see the single-CTA stream-K kernel).
-  e = launch_pdl(kfn, dim3(2u * unsigned(k.clusters)), dim3(tc::kThreads), smem, st, m[0], m[1], m[2], m[3], m[4], k);
+  // Programmatic dependent of the Gram reduce (see the single-CTA stream-K kernel), or an
+  // ordinary launch that waits for everything before it.
+  if (plain) {
+    kfn<<<dim3(2u * unsigned(k.clusters)), dim3(tc::kThreads), smem, st>>>(m[0], m[1], m[2], m[3], m[4], k);
+    e = cudaSuccess;
+  } else {
+    e = launch_pdl(kfn, dim3(2u * unsigned(k.clusters)), dim3(tc::kThreads), smem, st, m[0], m[1], m[2], m[3], m[4],
+                   k);
+  }
   if (e != cudaSuccess) return set_cuda_error(e);
   return check_launch();
 }
@@ -537,6 +552,7 @@ int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   if (fuse && (!tc::make_map(&maps[3], a.G1, a.dtype, a.N, a.N, hb) ||
                !tc::make_map(&maps[4], a.G2, a.dtype, a.N, a.N, hb)))
     return DORA_ERR_CUDA;
+  if (a.Y2 && !tc::make_map(&maps[4], a.Y2, a.dtype, a.N, a.K, hb)) return DORA_ERR_CUDA;
   const tc::Sk2Layout L = tc::sk2_layout(sh.nt, fuse);
   tc::Sk2Args k{};
   k.M = a.M;
@@ -545,6 +561,8 @@ int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.pair_tiles = int((a.M + 2 * tc::BM - 1) / (2 * tc::BM));
   k.ksub = L.ksub;
   k.kblocks = (sh.kblocks + L.ksub - 1) / L.ksub;  // units of ksub k-blocks
+  k.y2_units = a.Y2 ? k.kblocks : 0;
+  if (a.Y2) k.kblocks *= 2;
   k.stages = L.stages;
   k.clusters = p.grid;
   k.slots = p.slots;
@@ -563,8 +581,8 @@ int tc2_sk_rowdot_gemm(const TcGemmArgs& a, const SkPlan& p, cudaStream_t st) {
   k.rowdot_part = a.rowdot_part;
   k.sumsq_part = a.sumsq_part;
   k.v_part = a.v_part;
-  if (a.dtype == DORA_DTYPE_BF16) return launch_sk2<__nv_bfloat16>(k, maps, L.total, st);
-  return launch_sk2<__half>(k, maps, L.total, st);
+  if (a.dtype == DORA_DTYPE_BF16) return launch_sk2<__nv_bfloat16>(k, maps, L.total, st, a.plain_launch);
+  return launch_sk2<__half>(k, maps, L.total, st, a.plain_launch);
 }
 
 }  // namespace dora
