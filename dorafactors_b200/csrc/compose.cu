@@ -14,8 +14,9 @@
 // the rows, so the slices of g (and bias) it needs are loaded once into
 // registers and reused for every row (no per-element g traffic, no index
 // division).  A warp covers 32 consecutive 16-byte slices of one row (512
-// contiguous bytes), and four rows are in flight per thread to keep enough
-// bytes outstanding to saturate HBM3e.  The grid is sized to the SM count.
+// contiguous bytes), and four rows are in flight per thread.  The grid is deep
+// (64 CTAs per SM's worth, so each thread covers only a few row groups and CTAs
+// retire and refill evenly) and the outputs use streaming stores.
 //
 // Arithmetic is fp32 with one rounding per output; the op order is the
 // reference's ((g - 1) * base + g * (s * lora), dora_fused.py:32-54, then
@@ -76,8 +77,8 @@ compose_fwd_kernel(const TA* lora, const TA* __restrict__ base, const TG* __rest
           Vec16<TA>::unpack(rv[u], bf);
 #pragma unroll
           for (int k = 0; k < VEC; ++k) one(lf[k], bf[k], k, of[k], inf[k]);
-          st_global(out + off, Vec16<TA>::pack(of));
-          if constexpr (kInner) st_global(inner + off, Vec16<TA>::pack(inf));
+          st_stream(out + off, Vec16<TA>::pack(of));
+          if constexpr (kInner) st_stream(inner + off, Vec16<TA>::pack(inf));
         }
       }
     } else {
@@ -133,7 +134,10 @@ static int launch_compose(const void* lora, const void* base, const void* g, con
                    (inner == nullptr || aligned16(inner));
   const int64_t vcols = vec ? cols / V : cols;
   if (vcols > int64_t(65535) * 64) return DORA_ERR_UNSUPPORTED;
-  EwShape sh = ew_shape(rows, vcols);
+  // A deep grid (up to 64 CTAs per SM, each thread a few row groups) with streaming
+  // stores: 16384 x 28672 layer-output form 0.633 -> 0.565 ms in a probe (5.9 -> 6.7
+  // TB/s, the copy rate), against 8 CTAs per SM and plain stores.
+  EwShape sh = ew_shape(rows, vcols, 64);
   const bool with_inner = inner != nullptr;
   const bool inplace = (out == lora);
 #define DORA_COMPOSE_LAUNCH(VV)                                                                                     \

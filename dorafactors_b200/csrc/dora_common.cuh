@@ -101,6 +101,13 @@ __device__ __forceinline__ void st_global(void* p, const uint4& v) {
                "r"(v.w)
                : "memory");
 }
+// Streaming store (evict-first in L2): outputs that the kernel never reads again and
+// that are far larger than L2.
+__device__ __forceinline__ void st_stream(void* p, const uint4& v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // Device error word: set by a kernel whose bounded wait expired.
