@@ -151,12 +151,24 @@ struct BwdPlan {
   size_t counter_bytes, partial_bytes;
 };
 
-static BwdPlan bwd_plan(int64_t rows, int64_t cols, int esize, bool aligned) {
+// Row-grid depth: about 40 rows per thread, between the depths of 8 and of 32 CTAs
+// per SM's worth.  Deeper grids balance the SMs better; every grid row adds a row of
+// column partials that the last CTA of each column tile folds at the end.  Same GPU,
+// layer-output form: 16384 x 28672 0.631 (8 per SM) / 0.617 (16) / 0.610 ms (32);
+// 8192 x 8192 0.1015 / 0.108 / 0.125 ms.  shallow = true keeps the 8-per-SM depth
+// (fewer partials, for a fixed-size scratch).
+static BwdPlan bwd_plan(int64_t rows, int64_t cols, int esize, bool aligned, bool shallow = false) {
   BwdPlan p;
   const int V = 16 / esize;
   p.vec = aligned && (cols % V == 0);
   p.vcols = p.vec ? cols / V : cols;
-  p.sh = ew_shape(rows, p.vcols);
+  p.sh = ew_shape(rows, p.vcols, 8);
+  if (!shallow) {
+    const int64_t deep = ew_shape(rows, p.vcols, 32).grid.y;
+    int64_t gy = rows / 160;
+    if (gy > deep) gy = deep;
+    if (gy > int64_t(p.sh.grid.y)) p.sh.grid.y = unsigned(gy);
+  }
   p.counter_bytes = ((size_t(p.sh.grid.x) * 4 + 255) / 256) * 256;
   p.partial_bytes = size_t(p.sh.grid.y) * size_t(cols) * 4;
   return p;
@@ -195,11 +207,11 @@ static void launch_bwd_sel(const BwdPlan& p, const void* d_out, const void* inne
 template <typename TA, typename TG, bool RG, bool LD = false>
 static int launch_bwd(const void* d_out, const void* inner, const void* g, float s, void* d_lora, void* d_base,
                       void* d_g, void* ws, size_t ws_bytes, int64_t rows, int64_t cols, cudaStream_t st,
-                      int64_t ld_d = 0) {
+                      int64_t ld_d = 0, bool shallow = false) {
   constexpr int V = 16 / sizeof(TA);
   const bool aligned = aligned16(d_out) && (!inner || aligned16(inner)) && (!d_lora || aligned16(d_lora)) &&
                        (!d_base || aligned16(d_base)) && (!LD || ld_d % V == 0);
-  BwdPlan p = bwd_plan(rows, cols, sizeof(TA), aligned);
+  BwdPlan p = bwd_plan(rows, cols, sizeof(TA), aligned, shallow);
   unsigned* cnt = nullptr;
   float* part = nullptr;
   if (d_g) {
@@ -231,7 +243,7 @@ namespace dora {
 template <bool RG, bool LD = false>
 static int bwd_entry(const void* d_out, const void* inner, const void* g, int g_dtype, double scale, void* d_lora,
                      void* d_base, void* d_g, void* workspace, size_t workspace_bytes, int64_t rows, int64_t cols,
-                     int act_dtype, void* stream, int64_t ld_d = 0) {
+                     int act_dtype, void* stream, int64_t ld_d = 0, bool shallow = false) {
   if (rows < 0 || cols < 0 || !dtype_ok(act_dtype) || !dtype_ok(g_dtype)) return DORA_ERR_INVALID_ARGUMENT;
   if (g_dtype != act_dtype && g_dtype != DORA_DTYPE_F32) return DORA_ERR_INVALID_ARGUMENT;
   if (LD && ld_d < cols) return DORA_ERR_INVALID_ARGUMENT;
@@ -254,18 +266,18 @@ static int bwd_entry(const void* d_out, const void* inner, const void* g, int g_
     case DORA_DTYPE_BF16:
       return g_dtype == DORA_DTYPE_F32
                  ? launch_bwd<__nv_bfloat16, float, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
-                                                            workspace_bytes, rows, cols, st, ld_d)
+                                                            workspace_bytes, rows, cols, st, ld_d, shallow)
                  : launch_bwd<__nv_bfloat16, __nv_bfloat16, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g,
-                                                                    workspace, workspace_bytes, rows, cols, st, ld_d);
+                                                                    workspace, workspace_bytes, rows, cols, st, ld_d, shallow);
     case DORA_DTYPE_F16:
       return g_dtype == DORA_DTYPE_F32
                  ? launch_bwd<__half, float, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
-                                                     workspace_bytes, rows, cols, st, ld_d)
+                                                     workspace_bytes, rows, cols, st, ld_d, shallow)
                  : launch_bwd<__half, __half, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g, workspace,
-                                                      workspace_bytes, rows, cols, st, ld_d);
+                                                      workspace_bytes, rows, cols, st, ld_d, shallow);
     default:
       return launch_bwd<float, float, RG, LD>(d_out, inner, g, s, d_lora, d_base, d_g, workspace, workspace_bytes,
-                                              rows, cols, st, ld_d);
+                                              rows, cols, st, ld_d, shallow);
   }
 }
 
@@ -438,8 +450,17 @@ extern "C" int dora_compose_bwd_noalloc(const void* d_out, const void* inner, co
     return dora_compose_bwd(d_out, inner, g, g_dtype, scale, d_lora, d_base, d_g, nullptr, 0, rows, cols,
                             act_dtype, stream);
   }
-  const size_t need = dora_compose_bwd_workspace_size(rows, cols, act_dtype);
-  if (need > kStaticScratchBytes) return DORA_ERR_WORKSPACE;
+  // The workspace entry point's grid when its column partials fit the fixed array,
+  // else the shallow one (8 CTAs per SM's worth); beyond that the shape is rejected.
+  auto need_at = [&](bool shallow) {
+    const BwdPlan a = bwd_plan(rows, cols, dtype_size(act_dtype), true, shallow);
+    const BwdPlan b = bwd_plan(rows, cols, dtype_size(act_dtype), false, shallow);
+    const size_t na = a.counter_bytes + a.partial_bytes, nb = b.counter_bytes + b.partial_bytes;
+    return na > nb ? na : nb;
+  };
+  bool shallow = false;
+  if (need_at(false) > kStaticScratchBytes) shallow = true;
+  if (need_at(true) > kStaticScratchBytes) return DORA_ERR_WORKSPACE;
   // The rest of dora_compose_bwd's argument checks run before the array is
   // touched, so a call that will be rejected queues nothing on it.
   if (!inner || !d_out || !g) return DORA_ERR_INVALID_ARGUMENT;
@@ -454,6 +475,6 @@ extern "C" int dora_compose_bwd_noalloc(const void* d_out, const void* inner, co
   const size_t counter_bytes = c_vec > c_any ? c_vec : c_any;
   cudaError_t e = cudaMemsetAsync(ws, 0, counter_bytes, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return set_cuda_error(e);
-  return dora_compose_bwd(d_out, inner, g, g_dtype, scale, d_lora, d_base, d_g, ws, kStaticScratchBytes, rows,
-                          cols, act_dtype, stream);
+  return bwd_entry<false>(d_out, inner, g, g_dtype, scale, d_lora, d_base, d_g, ws, kStaticScratchBytes, rows, cols,
+                          act_dtype, stream, 0, shallow);
 }

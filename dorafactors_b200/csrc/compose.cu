@@ -134,10 +134,18 @@ static int launch_compose(const void* lora, const void* base, const void* g, con
                    (inner == nullptr || aligned16(inner));
   const int64_t vcols = vec ? cols / V : cols;
   if (vcols > int64_t(65535) * 64) return DORA_ERR_UNSUPPORTED;
-  // A deep grid (up to 64 CTAs per SM, each thread a few row groups) with streaming
-  // stores: 16384 x 28672 layer-output form 0.633 -> 0.565 ms in a probe (5.9 -> 6.7
-  // TB/s, the copy rate), against 8 CTAs per SM and plain stores.
-  EwShape sh = ew_shape(rows, vcols, 64);
+  // A deep grid with streaming stores: up to 64 CTAs per SM's worth, but each thread
+  // keeps at least three groups of four rows, and never fewer CTAs than 8 per SM's
+  // worth.  Same GPU, layer-output form: 16384 x 28672 0.612 (8 per SM) / 0.589 (16) /
+  // 0.570 ms (64); 8192 x 8192 0.0904 / 0.0894 / 0.0959 ms (64 leaves each thread less
+  // than one group of rows).
+  EwShape sh = ew_shape(rows, vcols, 8);
+  {
+    const EwShape deep = ew_shape(rows, vcols, 64);
+    const int64_t cap = rows / (int64_t(sh.block.y) * 4 * 3);
+    const int64_t gy = deep.grid.y < cap ? int64_t(deep.grid.y) : cap;
+    if (gy > int64_t(sh.grid.y)) sh.grid.y = unsigned(gy);
+  }
   const bool with_inner = inner != nullptr;
   const bool inplace = (out == lora);
 #define DORA_COMPOSE_LAUNCH(VV)                                                                                     \

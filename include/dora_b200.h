@@ -276,11 +276,14 @@ int dora_compose_bwd_channels(const void* d_out, const void* inner, const void* 
  * synchronizes the device.  Same arguments and results as dora_compose_bwd,
  * minus the workspace; no cudaMalloc, cudaFree or other allocating call is
  * made.  The scratch is a fixed DORA_NOALLOC_SCRATCH_BYTES array inside the
- * library's device image; a shape whose dora_compose_bwd_workspace_size()
- * exceeds it is rejected with DORA_ERR_WORKSPACE before anything is queued.
- * That size depends on the current device's SM count (the backward's grid),
- * so the largest accepted shape does too.  Argument errors are reported
- * before the array is touched.
+ * library's device image.  The backward's grid is the one dora_compose_bwd
+ * uses when its dora_compose_bwd_workspace_size() fits the array, else a
+ * shallower one (fewer column partials; d_g then differs from
+ * dora_compose_bwd's in fp32 summation order only); a shape whose partials fit
+ * neither is rejected with DORA_ERR_WORKSPACE before anything is queued.  The
+ * sizes depend on the current device's SM count (the backward's grid), so the
+ * largest accepted shape does too.  Argument errors are reported before the
+ * array is touched.
  *
  * The first call on each device looks up the array's device address (with
  * that device current) and caches it; make that first call before any stream
