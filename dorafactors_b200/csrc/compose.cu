@@ -139,13 +139,7 @@ static int launch_compose(const void* lora, const void* base, const void* g, con
   // worth.  Same GPU, layer-output form: 16384 x 28672 0.612 (8 per SM) / 0.589 (16) /
   // 0.570 ms (64); 8192 x 8192 0.0904 / 0.0894 / 0.0959 ms (64 leaves each thread less
   // than one group of rows).
-  EwShape sh = ew_shape(rows, vcols, 8);
-  {
-    const EwShape deep = ew_shape(rows, vcols, 64);
-    const int64_t cap = rows / (int64_t(sh.block.y) * 4 * 3);
-    const int64_t gy = deep.grid.y < cap ? int64_t(deep.grid.y) : cap;
-    if (gy > int64_t(sh.grid.y)) sh.grid.y = unsigned(gy);
-  }
+  EwShape sh = ew_shape_deep(rows, vcols);
   const bool with_inner = inner != nullptr;
   const bool inplace = (out == lora);
 #define DORA_COMPOSE_LAUNCH(VV)                                                                                     \

@@ -189,4 +189,16 @@ inline EwShape ew_shape(int64_t rows, int64_t vcols, int ctas_per_sm = 8) {
   return sh;
 }
 
+// Grid of the streaming elementwise kernels whose threads walk down the rows in
+// groups of four: deep (up to 64 CTAs per SM's worth, so CTAs retire and refill evenly)
+// but with at least three row groups per thread, and never shallower than 8 per SM.
+inline EwShape ew_shape_deep(int64_t rows, int64_t vcols) {
+  EwShape sh = ew_shape(rows, vcols, 8);
+  const EwShape deep = ew_shape(rows, vcols, 64);
+  const int64_t cap = rows / (int64_t(sh.block.y) * 4 * 3);
+  const int64_t gy = int64_t(deep.grid.y) < cap ? int64_t(deep.grid.y) : cap;
+  if (gy > int64_t(sh.grid.y)) sh.grid.y = unsigned(gy);
+  return sh;
+}
+
 }  // namespace dora
