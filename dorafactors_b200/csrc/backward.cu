@@ -71,8 +71,10 @@ compose_bwd_kernel(const TA* __restrict__ d_out, const TA* __restrict__ inner, c
               if constexpr (kDB) bf[k] = __fmul_rn(gm1[k], df[k]);
               if constexpr (kDG) acc[k] = fmaf(xf[k], df[k], acc[k]);
             }
-            if constexpr (kDL) st_global(d_lora + off, Vec16<TA>::pack(lf));
-            if constexpr (kDB) st_global(d_base + off, Vec16<TA>::pack(bf));
+            // Streaming stores (evict-first): same GPU, 16384 x 28672 0.6075 -> 0.6031 ms,
+            // 8192 x 8192 0.1015 -> 0.0985 ms.
+            if constexpr (kDL) st_stream(d_lora + off, Vec16<TA>::pack(lf));
+            if constexpr (kDB) st_stream(d_base + off, Vec16<TA>::pack(bf));
           }
         }
       } else {
